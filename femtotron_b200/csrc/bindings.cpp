@@ -1,0 +1,51 @@
+// Python bindings of the femtotron_b200 native extension (module femtotron_b200._C).
+#include <torch/extension.h>
+
+namespace ft {
+void gemm_tc(const torch::Tensor& A, const torch::Tensor& B, torch::Tensor& D, bool a_mn,
+             bool b_mn, int64_t mode, const c10::optional<torch::Tensor>& R,
+             const c10::optional<torch::Tensor>& GU, int64_t gate_up_off, torch::Tensor& err);
+void rmsnorm_fwd(const torch::Tensor& x, const torch::Tensor& w, torch::Tensor& y,
+                 torch::Tensor& rstd, double eps);
+void rmsnorm_bwd(const torch::Tensor& dy, const torch::Tensor& x, const torch::Tensor& w,
+                 const torch::Tensor& rstd, torch::Tensor& dx, torch::Tensor& dw_acc);
+void rope_apply(torch::Tensor& qk, const torch::Tensor& cos_t, const torch::Tensor& sin_t,
+                const c10::optional<torch::Tensor>& pos, int64_t nheads, int64_t head_dim,
+                int64_t seq_len, bool inverse);
+void swiglu_fwd(const torch::Tensor& gu, torch::Tensor& h, int64_t F);
+void swiglu_bwd(const torch::Tensor& dh, const torch::Tensor& gu, torch::Tensor& dgu, int64_t F);
+void xent_stats(const torch::Tensor& logits, const torch::Tensor& labels, torch::Tensor& stats,
+                int64_t vstart);
+void xent_bwd(torch::Tensor& logits, const torch::Tensor& labels, const torch::Tensor& lse,
+              const torch::Tensor& grad_scale, int64_t vstart, int64_t ignore_index);
+void embed_fwd(const torch::Tensor& ids, const torch::Tensor& table, torch::Tensor& out,
+               int64_t vstart);
+void embed_bwd(const torch::Tensor& ids, const torch::Tensor& dout, torch::Tensor& dtable,
+               int64_t vstart);
+void adamw_multi(const std::vector<torch::Tensor>& params, const std::vector<torch::Tensor>& ms,
+                 const std::vector<torch::Tensor>& vs, const std::vector<torch::Tensor>& grads,
+                 const std::vector<torch::Tensor>& p16s, const std::vector<double>& wds,
+                 double lr, double beta1, double beta2, double eps, int64_t step,
+                 const c10::optional<torch::Tensor>& grad_scale);
+void sumsq_multi(const std::vector<torch::Tensor>& xs, const std::vector<int64_t>& slots,
+                 torch::Tensor& out);
+void clip_coef(const torch::Tensor& sumsq, torch::Tensor& norm_out, torch::Tensor& coef_out,
+               double max_norm, double extra_scale);
+}  // namespace ft
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "femtotron_b200 sm_100a kernels";
+  m.def("gemm_tc", &ft::gemm_tc, "tcgen05 GEMM with fused epilogues");
+  m.def("rmsnorm_fwd", &ft::rmsnorm_fwd);
+  m.def("rmsnorm_bwd", &ft::rmsnorm_bwd);
+  m.def("rope_apply", &ft::rope_apply);
+  m.def("swiglu_fwd", &ft::swiglu_fwd);
+  m.def("swiglu_bwd", &ft::swiglu_bwd);
+  m.def("xent_stats", &ft::xent_stats);
+  m.def("xent_bwd", &ft::xent_bwd);
+  m.def("embed_fwd", &ft::embed_fwd);
+  m.def("embed_bwd", &ft::embed_bwd);
+  m.def("adamw_multi", &ft::adamw_multi);
+  m.def("sumsq_multi", &ft::sumsq_multi);
+  m.def("clip_coef", &ft::clip_coef);
+}

@@ -1,0 +1,477 @@
+// Persistent tcgen05 GEMM for sm_100a.
+//
+//   D[M,N] (op)= A[M,K] * B[N,K]^T      (fp32 accumulation in TMEM, bf16 operands)
+//
+// A and B may each be K-major (row-major with K contiguous) or MN-major (K rows, M/N
+// contiguous), so one kernel covers the three linear-layer products:
+//   forward  Y  = X  W^T : A = X  (K-major),  B = W  (K-major)
+//   dgrad    dX = dY W   : A = dY (K-major),  B = W  (MN-major)
+//   wgrad    dW = dY^T X : A = dY (MN-major), B = X  (MN-major)
+//
+// Structure (one CTA per SM, persistent over output tiles):
+//   warp 0      TMA producer: one lane streams A/B k-blocks into a STAGES-deep smem ring.
+//   warp 1      MMA issuer:   one lane issues tcgen05.mma (M=128, N=BN, K=16) into one of two
+//                             TMEM accumulators and commits to mbarriers.
+//   warp 2      TMEM allocator (512 columns = two BN<=256 fp32 accumulators).
+//   warps 4..7  epilogue: tcgen05.ld of their 32 TMEM lanes, fused epilogue op, global store.
+// The double-buffered accumulator lets the epilogue of tile i overlap the MMAs of tile i+1.
+// No TMA multicast is used anywhere (each CTA loads its own tiles).
+//
+// Fused epilogues: plain bf16/fp32 store, in-place accumulation into an fp32 or bf16
+// gradient buffer (wgrad of gradient accumulation), residual add (o_proj / down_proj), and
+// SwiGLU (gate/up projection: the B tile pairs 128 gate rows with the matching 128 up rows).
+//
+// Every mbarrier wait is bounded by a wall-clock limit; on expiry the kernel records an error
+// code in `err` and leaves its loops, so a bug cannot spin a GPU forever.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include "common.cuh"
+#include "tmap.h"
+
+namespace ft {
+namespace gemm {
+
+constexpr int BM = 128;
+constexpr int BK = 64;  // 64 bf16 = 128 bytes = one SW128 row
+constexpr int NUM_THREADS = 256;
+constexpr int EPI_WARP0 = 4;
+
+enum EpiMode : int {
+  EPI_STORE_BF16 = 0,   // D = acc (bf16)
+  EPI_STORE_F32 = 1,    // D = acc (fp32)
+  EPI_ACC_F32 = 2,      // D += acc (fp32)
+  EPI_ACC_BF16 = 3,     // D += acc (bf16 storage, fp32 math)
+  EPI_RESID_BF16 = 4,   // D = acc + R (bf16)
+  EPI_SWIGLU_BF16 = 5,  // tile = [gate 128 | up 128]: D = silu(g)*u, and g,u stored to GU
+};
+
+struct Params {
+  int M, N, K;
+  void* D;
+  int64_t ldd;
+  const __nv_bfloat16* R;  // residual (EPI_RESID_BF16)
+  int64_t ldr;
+  __nv_bfloat16* GU;       // gate/up pre-activations (EPI_SWIGLU_BF16): [M, gate_up_off + N]
+  int64_t ldgu;
+  int mode;
+  int gate_up_off;         // EPI_SWIGLU_BF16: first row of the up block inside B
+  int group_m;
+  int* err;
+};
+
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Bounded mbarrier wait: about two seconds of wall clock, then record `code` and give up.
+__device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, int* err, int code) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 128; ++i)
+      if (mbar_try_wait(bar, parity)) return true;
+    if (global_ns() - t0 > 2000000000ull) {
+      if (err) atomicExch(err, code);
+      return false;
+    }
+  }
+}
+
+// Grouped tile order: walk group_m row-tiles down a column before moving right, so one
+// wave of CTAs touches few A row-panels and few B column-panels (L2 reuse).
+__device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int group_m,
+                                            int& tm, int& tn) {
+  const int per_group = group_m * tiles_n;
+  const int g = t / per_group;
+  const int first_m = g * group_m;
+  const int gsize = min(tiles_m - first_m, group_m);
+  const int r = t - g * per_group;
+  tm = first_m + (r % gsize);
+  tn = r / gsize;
+}
+
+template <int BN, int STAGES>
+struct Smem {
+  __nv_bfloat16 a[STAGES][BM * BK];
+  __nv_bfloat16 b[STAGES][BN * BK];
+  uint64_t full[STAGES];
+  uint64_t empty[STAGES];
+  uint64_t acc_full[2];
+  uint64_t acc_empty[2];
+  uint32_t tmem_base;
+};
+
+__device__ __forceinline__ void store_bf16x32(__nv_bfloat16* dst, const float* v, int valid) {
+  // valid: number of valid columns (multiple of 8) starting at dst.
+  uint32_t pk[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) pk[i] = pack_bf16x2(v[2 * i], v[2 * i + 1]);
+  uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    if (j * 8 < valid) d4[j] = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+}
+
+__device__ __forceinline__ void load_bf16x32(const __nv_bfloat16* src, float* v, int valid) {
+  const uint4* s4 = reinterpret_cast<const uint4*>(src);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    uint4 q = (j * 8 < valid) ? s4[j] : make_uint4(0, 0, 0, 0);
+    float2 f;
+    f = unpack_bf16x2(q.x); v[8 * j + 0] = f.x; v[8 * j + 1] = f.y;
+    f = unpack_bf16x2(q.y); v[8 * j + 2] = f.x; v[8 * j + 3] = f.y;
+    f = unpack_bf16x2(q.z); v[8 * j + 4] = f.x; v[8 * j + 5] = f.y;
+    f = unpack_bf16x2(q.w); v[8 * j + 6] = f.x; v[8 * j + 7] = f.y;
+  }
+}
+
+template <bool A_MN, bool B_MN, int BN, int STAGES>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
+                const Params p) {
+  using S = Smem<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  S& s = *reinterpret_cast<S*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const bool swiglu = (p.mode == EPI_SWIGLU_BF16);
+  const int out_cols = swiglu ? (BN / 2) : BN;  // output columns per tile
+  const int tiles_m = (p.M + BM - 1) / BM;
+  const int tiles_n = (p.N + out_cols - 1) / out_cols;
+  const int num_tiles = tiles_m * tiles_n;
+  const int kblocks = (p.K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int i = 0; i < STAGES; ++i) {
+      mbar_init(&s.full[i], 1);
+      mbar_init(&s.empty[i], 1);
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s.acc_full[i], 1);
+      mbar_init(&s.acc_empty[i], 4);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 2) {
+    tmem_alloc(&s.tmem_base, 512);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tma_a);
+    prefetch_tmap(&tma_b);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s.tmem_base;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        int tm, tn;
+        tile_coords(t, tiles_m, tiles_n, p.group_m, tm, tn);
+        const int m0 = tm * BM;
+        const int n0 = tn * out_cols;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!wait_bar(&s.empty[stage], phase ^ 1, p.err, 1)) { ok = false; break; }
+          mbar_arrive_expect_tx(&s.full[stage], (BM + BN) * BK * 2);
+          const int k0 = kb * BK;
+          if (!A_MN) {
+            tma_load_2d(s.a[stage], &tma_a, &s.full[stage], k0, m0);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BM / 64; ++j)
+              tma_load_2d(s.a[stage] + j * 64 * BK, &tma_a, &s.full[stage], m0 + 64 * j, k0);
+          }
+          if (!B_MN) {
+            if (swiglu) {
+              tma_load_2d(s.b[stage], &tma_b, &s.full[stage], k0, n0);
+              tma_load_2d(s.b[stage] + (BN / 2) * BK, &tma_b, &s.full[stage], k0,
+                          p.gate_up_off + n0);
+            } else {
+              tma_load_2d(s.b[stage], &tma_b, &s.full[stage], k0, n0);
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j)
+              tma_load_2d(s.b[stage] + j * 64 * BK, &tma_b, &s.full[stage], n0 + 64 * j, k0);
+          }
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (elect_one()) {
+      constexpr uint32_t idesc = make_idesc_bf16(BM, BN, A_MN, B_MN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        if (!wait_bar(&s.acc_empty[acc], acc_phase ^ 1, p.err, 2)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem + acc * BN;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!wait_bar(&s.full[stage], phase, p.err, 3)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(s.a[stage]);
+          const uint32_t b_base = smem_u32(s.b[stage]);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t ad = A_MN ? make_sw128_desc(a_base + kk * 2048, 64 * BK * 2, 1024)
+                                     : make_sw128_desc(a_base + kk * 32, 16, 1024);
+            const uint64_t bd = B_MN ? make_sw128_desc(b_base + kk * 2048, 64 * BK * 2, 1024)
+                                     : make_sw128_desc(b_base + kk * 32, 16, 1024);
+            mma_bf16(d_tmem, ad, bd, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+          }
+          mma_commit(&s.empty[stage]);
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        mma_commit(&s.acc_full[acc]);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1;
+      }
+    }
+  } else if (warp >= EPI_WARP0) {
+    // ---------------- Epilogue ----------------
+    const int q = warp - EPI_WARP0;  // TMEM lane quadrant owned by this warp
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+      int tm, tn;
+      tile_coords(t, tiles_m, tiles_n, p.group_m, tm, tn);
+      const int m0 = tm * BM;
+      const int n0 = tn * out_cols;
+      if (!wait_bar(&s.acc_full[acc], acc_phase, p.err, 4)) break;
+      tc_fence_after();
+      const int row = m0 + q * 32 + lane;
+      const bool row_ok = row < p.M;
+      const uint32_t tbase = tmem + acc * BN + (static_cast<uint32_t>(q * 32) << 16);
+
+      if (!swiglu) {
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tbase + c * 32, r);
+          tmem_wait_ld();
+          const int col0 = n0 + c * 32;
+          const int valid = min(32, p.N - col0);
+          if (row_ok && valid > 0) {
+            float v[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+            if (p.mode == EPI_STORE_BF16 || p.mode == EPI_RESID_BF16 || p.mode == EPI_ACC_BF16) {
+              __nv_bfloat16* d = reinterpret_cast<__nv_bfloat16*>(p.D) + (int64_t)row * p.ldd + col0;
+              if (p.mode != EPI_STORE_BF16) {
+                float o[32];
+                if (p.mode == EPI_RESID_BF16)
+                  load_bf16x32(p.R + (int64_t)row * p.ldr + col0, o, valid);
+                else
+                  load_bf16x32(d, o, valid);
+#pragma unroll
+                for (int i = 0; i < 32; ++i) v[i] += o[i];
+              }
+              store_bf16x32(d, v, valid);
+            } else {
+              float* d = reinterpret_cast<float*>(p.D) + (int64_t)row * p.ldd + col0;
+              float4* d4 = reinterpret_cast<float4*>(d);
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                if (j * 4 < valid) {
+                  float4 x = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+                  if (p.mode == EPI_ACC_F32) {
+                    float4 o = d4[j];
+                    x.x += o.x; x.y += o.y; x.z += o.z; x.w += o.w;
+                  }
+                  d4[j] = x;
+                }
+              }
+            }
+          }
+        }
+      } else {
+        constexpr int HALF = BN / 2;
+#pragma unroll 1
+        for (int c = 0; c < HALF / 32; ++c) {
+          uint32_t rg[32], ru[32];
+          tmem_ld_32x32b_x32(tbase + c * 32, rg);
+          tmem_ld_32x32b_x32(tbase + HALF + c * 32, ru);
+          tmem_wait_ld();
+          const int col0 = n0 + c * 32;
+          const int valid = min(32, p.N - col0);
+          if (row_ok && valid > 0) {
+            float g[32], u[32], h[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              g[i] = __uint_as_float(rg[i]);
+              u[i] = __uint_as_float(ru[i]);
+              // Round the pre-activations to bf16 first so the forward matches what the
+              // backward (which reads the stored bf16 g,u) differentiates.
+              const float gb = __bfloat162float(__float2bfloat16_rn(g[i]));
+              const float ub = __bfloat162float(__float2bfloat16_rn(u[i]));
+              h[i] = gb / (1.0f + __expf(-gb)) * ub;
+            }
+            __nv_bfloat16* d = reinterpret_cast<__nv_bfloat16*>(p.D) + (int64_t)row * p.ldd + col0;
+            store_bf16x32(d, h, valid);
+            __nv_bfloat16* gu = p.GU + (int64_t)row * p.ldgu;
+            store_bf16x32(gu + col0, g, valid);
+            store_bf16x32(gu + p.gate_up_off + col0, u, valid);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s.acc_empty[acc]);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ------------------------------------------------------------------------------------------
+// Host launcher
+// ------------------------------------------------------------------------------------------
+static int num_sms() {
+  static int n = 0;
+  if (n == 0) {
+    int dev;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return n;
+}
+
+template <bool A_MN, bool B_MN, int BN, int STAGES>
+static void launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, int num_tiles,
+                   cudaStream_t stream) {
+  auto kern = gemm_kernel<A_MN, B_MN, BN, STAGES>;
+  const int smem = static_cast<int>(sizeof(Smem<BN, STAGES>)) + 1024;
+  static bool configured = false;  // one flag per template instance
+  if (!configured) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    configured = true;
+  }
+  const int grid = std::max(1, std::min(num_tiles, num_sms()));
+  kern<<<grid, NUM_THREADS, smem, stream>>>(ta, tb, p);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+template <bool A_MN, bool B_MN>
+static void dispatch_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tb, const Params& p,
+                        int num_tiles, cudaStream_t stream) {
+  if (bn == 256)
+    launch<A_MN, B_MN, 256, 4>(ta, tb, p, num_tiles, stream);
+  else
+    launch<A_MN, B_MN, 128, 6>(ta, tb, p, num_tiles, stream);
+}
+
+// Pick BN in {128, 256} by estimated wave-quantised time (tiles per SM * BN).
+static int choose_bn(int M, int N, bool swiglu) {
+  if (swiglu) return 256;
+  const int sms = num_sms();
+  const int tm = (M + BM - 1) / BM;
+  const int t256 = tm * ((N + 255) / 256), t128 = tm * ((N + 127) / 128);
+  const long c256 = (long)((t256 + sms - 1) / sms) * 256;
+  const long c128 = (long)((t128 + sms - 1) / sms) * 128;
+  return (c256 <= c128) ? 256 : 128;
+}
+
+}  // namespace gemm
+
+// A: [M,K] (a_mn=false) or [K,M] (a_mn=true); B: [N,K] (b_mn=false) or [K,N] (b_mn=true).
+// D: [M,N] bf16 or fp32 per `mode`.  All operands row-major with unit inner stride.
+void gemm_tc(const torch::Tensor& A, const torch::Tensor& B, torch::Tensor& D, bool a_mn,
+             bool b_mn, int64_t mode, const c10::optional<torch::Tensor>& R,
+             const c10::optional<torch::Tensor>& GU, int64_t gate_up_off, torch::Tensor& err) {
+  using namespace gemm;
+  TORCH_CHECK(A.is_cuda() && B.is_cuda() && D.is_cuda(), "gemm_tc: CUDA tensors required");
+  TORCH_CHECK(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16,
+              "gemm_tc: bf16 operands required");
+  TORCH_CHECK(A.dim() == 2 && B.dim() == 2 && D.dim() == 2, "gemm_tc: 2-D operands required");
+  TORCH_CHECK(A.stride(1) == 1 && B.stride(1) == 1 && D.stride(1) == 1,
+              "gemm_tc: unit inner stride required");
+  const int M = a_mn ? A.size(1) : A.size(0);
+  const int K = a_mn ? A.size(0) : A.size(1);
+  const bool swiglu = (mode == EPI_SWIGLU_BF16);
+  const int N = D.size(1);
+  const int Kb = b_mn ? B.size(0) : B.size(1);
+  TORCH_CHECK(K == Kb, "gemm_tc: K mismatch ", K, " vs ", Kb);
+  TORCH_CHECK(D.size(0) == M, "gemm_tc: D rows mismatch");
+  if (swiglu) {
+    TORCH_CHECK(!b_mn, "gemm_tc: swiglu epilogue needs a K-major B");
+    TORCH_CHECK(B.size(0) >= gate_up_off + N, "gemm_tc: swiglu B too small");
+    TORCH_CHECK(GU.has_value() && GU->size(0) == M && GU->size(1) >= gate_up_off + N,
+                "gemm_tc: swiglu needs GU [M, gate_up_off+N]");
+    TORCH_CHECK(N % 8 == 0 && gate_up_off % 8 == 0, "gemm_tc: swiglu sizes must be multiples of 8");
+  } else {
+    const int Nb = b_mn ? B.size(1) : B.size(0);
+    TORCH_CHECK(Nb == N, "gemm_tc: N mismatch ", Nb, " vs ", N);
+  }
+  TORCH_CHECK(N % 8 == 0, "gemm_tc: N must be a multiple of 8");
+  const bool out_f32 = (mode == EPI_STORE_F32 || mode == EPI_ACC_F32);
+  TORCH_CHECK(D.scalar_type() == (out_f32 ? at::kFloat : at::kBFloat16), "gemm_tc: D dtype");
+  TORCH_CHECK(D.stride(0) % (out_f32 ? 4 : 8) == 0 &&
+                  reinterpret_cast<uintptr_t>(D.data_ptr()) % 16 == 0,
+              "gemm_tc: D must be 16-byte aligned with an aligned row stride");
+  if (mode == EPI_RESID_BF16) {
+    TORCH_CHECK(R.has_value() && R->scalar_type() == at::kBFloat16 && R->size(0) == M &&
+                    R->size(1) == N && R->stride(1) == 1 && R->stride(0) % 8 == 0,
+                "gemm_tc: bad residual");
+  }
+  const c10::cuda::CUDAGuard guard(A.device());
+  auto stream = at::cuda::getCurrentCUDAStream();
+
+  const int bn = choose_bn(M, N, swiglu);
+  const auto BF16 = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  CUtensorMap ta = a_mn ? make_tmap_2d(A.data_ptr(), BF16, 2, M, K, A.stride(0), 64, 64, true)
+                        : make_tmap_2d(A.data_ptr(), BF16, 2, K, M, A.stride(0), 64, BM, true);
+  CUtensorMap tb;
+  if (b_mn)
+    tb = make_tmap_2d(B.data_ptr(), BF16, 2, B.size(1), K, B.stride(0), 64, 64, true);
+  else
+    tb = make_tmap_2d(B.data_ptr(), BF16, 2, K, B.size(0), B.stride(0), 64, swiglu ? 128 : bn,
+                      true);
+
+  Params p;
+  p.M = M; p.N = N; p.K = K;
+  p.D = D.data_ptr(); p.ldd = D.stride(0);
+  p.R = R.has_value() ? reinterpret_cast<const __nv_bfloat16*>(R->data_ptr()) : nullptr;
+  p.ldr = R.has_value() ? R->stride(0) : 0;
+  p.GU = GU.has_value() ? reinterpret_cast<__nv_bfloat16*>(GU->data_ptr()) : nullptr;
+  p.ldgu = GU.has_value() ? GU->stride(0) : 0;
+  p.mode = static_cast<int>(mode);
+  p.gate_up_off = static_cast<int>(gate_up_off);
+  p.group_m = 8;
+  p.err = err.data_ptr<int>();
+
+  const int out_cols = swiglu ? bn / 2 : bn;
+  const int num_tiles = ((M + BM - 1) / BM) * ((N + out_cols - 1) / out_cols);
+  if (!a_mn && !b_mn) dispatch_bn<false, false>(bn, ta, tb, p, num_tiles, stream);
+  else if (!a_mn && b_mn) dispatch_bn<false, true>(bn, ta, tb, p, num_tiles, stream);
+  else if (a_mn && b_mn) dispatch_bn<true, true>(bn, ta, tb, p, num_tiles, stream);
+  else dispatch_bn<true, false>(bn, ta, tb, p, num_tiles, stream);
+}
+
+}  // namespace ft

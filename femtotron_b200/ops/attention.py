@@ -1,0 +1,38 @@
+"""Causal GQA attention entry point.
+
+``flash_attention`` runs the sm_100a flash-attention kernels (forward and backward) on a
+packed [B*S, (nq+2nkv)*d] QKV projection.  Until those kernels are registered for a head
+size, ``flash_available`` is False and the caller uses PyTorch SDPA.
+"""
+from __future__ import annotations
+
+import torch
+
+from .ext import has_native, native
+
+
+def flash_available(head_dim: int) -> bool:
+    return has_native() and hasattr(native(), "flash_fwd") and head_dim in (64, 128)
+
+
+class FlashAttnFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, qkv, B, S, nq, nkv, d):
+        o = torch.empty(B * S, nq * d, dtype=qkv.dtype, device=qkv.device)
+        lse = torch.empty(B, nq, S, dtype=torch.float32, device=qkv.device)
+        native().flash_fwd(qkv, o, lse, B, S, nq, nkv, d)
+        ctx.save_for_backward(qkv, o, lse)
+        ctx.meta = (B, S, nq, nkv, d)
+        return o
+
+    @staticmethod
+    def backward(ctx, do):
+        qkv, o, lse = ctx.saved_tensors
+        B, S, nq, nkv, d = ctx.meta
+        dqkv = torch.empty_like(qkv)
+        native().flash_bwd(qkv, o, do.contiguous(), lse, dqkv, B, S, nq, nkv, d)
+        return dqkv, None, None, None, None, None
+
+
+def flash_attention(qkv, B, S, nq, nkv, d):
+    return FlashAttnFn.apply(qkv, B, S, nq, nkv, d)

@@ -1,0 +1,202 @@
+"""ZeRO-3: parameters, gradients and optimizer state sharded over data parallelism.
+
+Units are chosen by a wrap policy (default: one per decoder block).  Each unit becomes a
+ParamGroupCluster and gets four module hooks (as in the reference,
+femtotron/sharding/zero3.py:191-226), with these B200-specific behaviours:
+  * forward-pre: unshard (consume the prefetched all-gather) and prefetch the NEXT unit on
+    the communication stream, so the gather overlaps the current unit's compute;
+  * forward-post: reshard — except during an activation-checkpoint recompute inside the
+    backward, where the parameters must stay until the unit's backward is done;
+  * backward-pre: unshard, allocate the transient gradient buffer, prefetch the PREVIOUS
+    unit;
+  * backward-post: reduce-scatter the unit's gradients on the communication stream
+    (skipped under ``no_sync``), then reshard.
+Parameters outside every unit (embedding, final norm, lm_head) keep unsharded fp32 masters
+and are all-reduced (AVG) at step time, like the reference.
+With dp_size == 1 the clusters run in direct mode (no hooks, no copies).
+"""
+from __future__ import annotations
+
+from contextlib import contextmanager
+
+import torch
+import torch.distributed as dist
+from torch import nn
+
+from .param_group_cluster import ParamGroupCluster
+
+
+class ZeRO3Strategy:
+    def __init__(self, dp_group, wrap_policy, prefetch: bool = True):
+        self.dp_group = dp_group
+        self.dp_rank = dist.get_rank(dp_group) if dp_group is not None else 0
+        self.dp_size = dist.get_world_size(dp_group) if dp_group is not None else 1
+        self.wrap_policy = wrap_policy
+        self.prefetch_enabled = prefetch
+        self.clusters: list[ParamGroupCluster] = []
+        self._hook_handles: list = []
+        self._sync_enabled = True
+        self.comm_stream = None
+
+    def make_master(self, compute: nn.Parameter, master_dtype: torch.dtype):
+        master = compute.detach().clone().to(master_dtype)
+        master.requires_grad_(True)
+        return master, None
+
+    def make_clusters(self, model: nn.Module, groups: list, master_dtype):
+        if master_dtype is None:
+            raise ValueError("ZeRO-3 requires a master_dtype (the optimizer state to shard)")
+        units = [m for m in model.modules() if self.wrap_policy(m)]
+        if not units:
+            raise RuntimeError("ZeRO-3 wrap_policy matched no module")
+        ids = {id(u) for u in units}
+        for u in units:
+            for sub in u.modules():
+                if sub is not u and id(sub) in ids:
+                    raise RuntimeError(f"nested ZeRO-3 units: {type(sub).__name__} inside {type(u).__name__}")
+        by_id = {id(pg.compute): pg for pg in groups}
+        dev = groups[0].compute.device if groups else torch.device("cpu")
+        if dev.type == "cuda" and self.dp_size > 1:
+            self.comm_stream = torch.cuda.Stream(device=dev)
+        names = {m: n for n, m in model.named_modules()}
+        for u in units:
+            pgs, seen = [], set()
+            for p in u.parameters():
+                if id(p) in seen:
+                    continue
+                seen.add(id(p))
+                pg = by_id.get(id(p))
+                if pg is None:
+                    continue
+                if pg.cluster is not None:
+                    raise RuntimeError(f"parameter {pg.name} claimed by two units")
+                pgs.append(pg)
+            if not pgs:
+                continue
+            c = ParamGroupCluster(names.get(u, type(u).__name__) or "<root>", u, pgs, self.dp_group,
+                                  master_dtype, comm_stream=self.comm_stream)
+            self.clusters.append(c)
+        for i, c in enumerate(self.clusters):
+            c.index = i
+            if not c.direct:
+                self._install_hooks(c)
+        # free (non-unit) parameters accumulate an fp32 gradient in place
+        for pg in groups:
+            if pg.cluster is None and pg.compute.requires_grad:
+                pg.compute.main_grad = torch.zeros(pg.compute.shape, dtype=torch.float32,
+                                                   device=pg.compute.device)
+        return self.clusters
+
+    # ------------------------------------------------------------------ hooks
+    def _install_hooks(self, c: ParamGroupCluster) -> None:
+        m = c.module
+        self._hook_handles += [
+            m.register_forward_pre_hook(lambda mod, args, c=c: self._pre_forward(c)),
+            m.register_forward_hook(lambda mod, args, out, c=c: self._post_forward(c)),
+            m.register_full_backward_pre_hook(lambda mod, go, c=c: self._pre_backward(c)),
+            m.register_full_backward_hook(lambda mod, gi, go, c=c: self._post_backward(c)),
+        ]
+
+    def _neighbor(self, c, step):
+        j = c.index + step
+        return self.clusters[j] if 0 <= j < len(self.clusters) else None
+
+    def _pre_forward(self, c):
+        c.unshard()
+        if self.prefetch_enabled and not c.in_backward:
+            n = self._neighbor(c, +1)
+            if n is not None:
+                n.prefetch()
+
+    def _post_forward(self, c):
+        if not c.in_backward:
+            c.reshard()
+
+    def _pre_backward(self, c):
+        c.in_backward = True
+        c.unshard()
+        c.prepare_grad_buffer()
+        if self.prefetch_enabled:
+            n = self._neighbor(c, -1)
+            if n is not None:
+                n.prefetch()
+
+    def _post_backward(self, c):
+        if self._sync_enabled:
+            c.reduce_scatter_grads()
+        c.reshard()
+        c.in_backward = False
+
+    # ------------------------------------------------------------------ strategy protocol
+    def prepare_for_backward(self, groups: list) -> None:
+        pass
+
+    def reduce_grads(self, compute_grads: list, targets: list, target_specs: list) -> list:
+        """Free parameters: all-reduce (AVG) over DP and return fp32 gradients."""
+        if self.comm_stream is not None:
+            torch.cuda.current_stream(self.comm_stream.device).wait_stream(self.comm_stream)
+        out = []
+        for g, t in zip(compute_grads, targets):
+            if g is None:
+                out.append(torch.zeros_like(t))
+                continue
+            if self.dp_size > 1:
+                dist.all_reduce(g, op=dist.ReduceOp.AVG, group=self.dp_group)
+            out.append(g if g.dtype == t.dtype else g.to(t.dtype))
+        return out
+
+    def wait_comm(self) -> None:
+        if self.comm_stream is not None:
+            torch.cuda.current_stream(self.comm_stream.device).wait_stream(self.comm_stream)
+
+    def gather_weights(self, groups: list) -> None:
+        for g in groups:
+            if g.master is not None:
+                with torch.no_grad():
+                    g.compute.copy_(g.master)
+
+    def post_step(self) -> None:
+        pass
+
+    def grads_are_dp_sharded(self) -> bool:
+        return True
+
+    @contextmanager
+    def no_sync(self):
+        prev = self._sync_enabled
+        self._sync_enabled = False
+        try:
+            yield
+        finally:
+            self._sync_enabled = prev
+
+    def sync_gradients(self) -> None:
+        pass
+
+    def state_dict(self) -> dict:
+        return {}
+
+    def load_state_dict(self, sd: dict) -> None:
+        pass
+
+    def force_reshard_all(self) -> None:
+        """Exception recovery: drop every gathered buffer and pending prefetch."""
+        for c in self.clusters:
+            try:
+                c._prefetch = None
+                c._grad_buffer = None
+                c.in_backward = False
+                c.reshard()
+            except Exception:
+                pass
+
+    def summary(self) -> dict:
+        return {"num_clusters": len(self.clusters),
+                "total_sharded_params": sum(c.total_numel for c in self.clusters),
+                "memory_per_cluster": [c.memory_footprint() for c in self.clusters]}
+
+    def cleanup(self) -> None:
+        for h in self._hook_handles:
+            h.remove()
+        self._hook_handles.clear()
+        self.clusters.clear()
