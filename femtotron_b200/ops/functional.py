@@ -19,7 +19,7 @@ import torch.distributed as dist
 from torch.autograd import Function
 
 from . import kernels as K
-from .gemm import gemm, linear_dgrad, linear_fwd, linear_wgrad
+from .matmul import gemm, linear_dgrad, linear_fwd, linear_wgrad
 
 
 # ------------------------------------------------------------------------------ helpers

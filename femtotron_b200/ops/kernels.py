@@ -96,7 +96,8 @@ def swiglu_bwd(dh: torch.Tensor, gu: torch.Tensor, F_: int, out: torch.Tensor | 
     if gu.is_cuda:
         native().swiglu_bwd(dh, gu, out, F_)
         return out
-    g, u, d = gu[:, :F_].float(), gu[:, F_:2 * F_].float(), dh.float()
+    # explicit copies: `out` may alias `gu`, and .float() does not copy fp32 inputs
+    g, u, d = gu[:, :F_].float().clone(), gu[:, F_:2 * F_].float().clone(), dh.float()
     s = torch.sigmoid(g)
     out[:, :F_] = (d * u * s * (1 + g * (1 - s))).to(gu.dtype)
     out[:, F_:2 * F_] = (d * g * s).to(gu.dtype)

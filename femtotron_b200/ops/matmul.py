@@ -34,7 +34,7 @@ def gemm(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor, *, a_mn: bool = Fa
         n = out.shape[1]
         g = A @ B[:n].t()
         u = A @ B[gate_up_off:gate_up_off + n].t()
-        gb, ub = g.to(torch.bfloat16), u.to(torch.bfloat16)
+        gb, ub = g.to(out.dtype), u.to(out.dtype)  # the kernel stores bf16 pre-activations
         gu[:, :n] = gb
         gu[:, gate_up_off:gate_up_off + n] = ub
         out.copy_(F.silu(gb.float()) * ub.float())

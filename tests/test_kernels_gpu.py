@@ -5,7 +5,7 @@ import pytest
 import torch
 import torch.nn.functional as F
 
-from femtotron_b200.ops import gemm as G
+from femtotron_b200.ops import matmul as G
 from femtotron_b200.ops import kernels as K
 from femtotron_b200.ops.ext import check_kernel_errors, native
 

@@ -25,7 +25,9 @@ def test_model_fwd_bwd_matches_fp32_cpu():
     cfg = _cfg()
     with torch.device("meta"):
         ref = LlamaForTraining(cfg)
-    materialize_model(ref, "cpu", dtype=torch.float32)
+    # HF-style init (norm weights 1, matrices N(0, 0.02)): well-conditioned gradients
+    init = lambda n, p: p.fill_(1.0) if p.dim() == 1 else p.normal_(0, 0.02)
+    materialize_model(ref, "cpu", dtype=torch.float32, init_fn=init)
     with torch.device("meta"):
         gpu = LlamaForTraining(cfg)
     materialize_model(gpu, "cuda", dtype=torch.bfloat16, init_std=None)
@@ -42,7 +44,7 @@ def test_model_fwd_bwd_matches_fp32_cpu():
     check_kernel_errors()
     assert abs(lg.item() - lr_.item()) < 2e-2 * abs(lr_.item())
     for (n, pg), pr in zip(gpu.named_parameters(), ref.parameters()):
-        assert rel(pg.grad.cpu(), pr.grad) < 8e-2, n
+        assert rel(pg.grad.cpu(), pr.grad) < 5e-2, n
 
 
 def test_zero3_training_runs_on_gpu():
