@@ -282,7 +282,8 @@ def run_reference(args):
         # the reference's own tests re-create rotary inv_freq after to_empty
         rot = model.model.rotary_emb
         dim = cfg.hidden_size // cfg.num_attention_heads
-        inv = 1.0 / (cfg.rope_theta ** (torch.arange(0, dim, 2, dtype=torch.int64).to(
+        theta = (getattr(cfg, "rope_parameters", None) or {}).get("rope_theta", 10000.0)
+        inv = 1.0 / (theta ** (torch.arange(0, dim, 2, dtype=torch.int64).to(
             device=device, dtype=torch.float) / dim))
         rot.inv_freq.copy_(inv)
         if hasattr(rot, "original_inv_freq"):

@@ -390,6 +390,11 @@ static void dispatch_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tb, co
 // Pick BN in {128, 256} by estimated wave-quantised time (tiles per SM * BN).
 static int choose_bn(int M, int N, bool swiglu) {
   if (swiglu) return 256;
+  static int forced = [] {
+    const char* e = getenv("FT_GEMM_BN");
+    return e ? atoi(e) : 0;
+  }();
+  if (forced == 128 || forced == 256) return forced;
   const int sms = num_sms();
   const int tm = (M + BM - 1) / BM;
   const int t256 = tm * ((N + 255) / 256), t128 = tm * ((N + 127) / 128);
