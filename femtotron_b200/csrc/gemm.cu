@@ -387,7 +387,8 @@ static void dispatch_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tb, co
     launch<A_MN, B_MN, 128, 6>(ta, tb, p, num_tiles, stream);
 }
 
-// Pick BN in {128, 256} by estimated wave-quantised time (tiles per SM * BN).
+// Pick BN: 256-wide tiles (better operand reuse per UMMA) unless N is small, measured
+// faster or equal on every Llama-3-8B projection shape; FT_GEMM_BN=128|256 forces one.
 static int choose_bn(int M, int N, bool swiglu) {
   if (swiglu) return 256;
   static int forced = [] {
@@ -395,12 +396,8 @@ static int choose_bn(int M, int N, bool swiglu) {
     return e ? atoi(e) : 0;
   }();
   if (forced == 128 || forced == 256) return forced;
-  const int sms = num_sms();
-  const int tm = (M + BM - 1) / BM;
-  const int t256 = tm * ((N + 255) / 256), t128 = tm * ((N + 127) / 128);
-  const long c256 = (long)((t256 + sms - 1) / sms) * 256;
-  const long c128 = (long)((t128 + sms - 1) / sms) * 128;
-  return (c256 <= c128) ? 256 : 128;
+  (void)M;
+  return N > 128 ? 256 : 128;
 }
 
 }  // namespace gemm
