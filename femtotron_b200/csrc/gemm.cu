@@ -130,6 +130,87 @@ __device__ __forceinline__ void load_bf16x32(const __nv_bfloat16* src, float* v,
   }
 }
 
+// Epilogue of one accumulator tile for the 32 rows of TMEM lane quadrant `q` (one row per
+// thread): read fp32 accumulators 32 columns at a time and apply the fused op.
+template <int BN>
+__device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t tmem_acc, int q, int lane,
+                                              int row, int n0, bool swiglu) {
+  const bool row_ok = row < p.M;
+  const uint32_t tbase = tmem_acc + (static_cast<uint32_t>(q * 32) << 16);
+
+      if (!swiglu) {
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tbase + c * 32, r);
+          tmem_wait_ld();
+          const int col0 = n0 + c * 32;
+          const int valid = min(32, p.N - col0);
+          if (row_ok && valid > 0) {
+            float v[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+            if (p.mode == EPI_STORE_BF16 || p.mode == EPI_RESID_BF16 || p.mode == EPI_ACC_BF16) {
+              __nv_bfloat16* d = reinterpret_cast<__nv_bfloat16*>(p.D) + (int64_t)row * p.ldd + col0;
+              if (p.mode != EPI_STORE_BF16) {
+                float o[32];
+                if (p.mode == EPI_RESID_BF16)
+                  load_bf16x32(p.R + (int64_t)row * p.ldr + col0, o, valid);
+                else
+                  load_bf16x32(d, o, valid);
+#pragma unroll
+                for (int i = 0; i < 32; ++i) v[i] += o[i];
+              }
+              store_bf16x32(d, v, valid);
+            } else {
+              float* d = reinterpret_cast<float*>(p.D) + (int64_t)row * p.ldd + col0;
+              float4* d4 = reinterpret_cast<float4*>(d);
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                if (j * 4 < valid) {
+                  float4 x = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+                  if (p.mode == EPI_ACC_F32) {
+                    float4 o = d4[j];
+                    x.x += o.x; x.y += o.y; x.z += o.z; x.w += o.w;
+                  }
+                  d4[j] = x;
+                }
+              }
+            }
+          }
+        }
+      } else {
+        constexpr int HALF = BN / 2;
+#pragma unroll 1
+        for (int c = 0; c < HALF / 32; ++c) {
+          uint32_t rg[32], ru[32];
+          tmem_ld_32x32b_x32(tbase + c * 32, rg);
+          tmem_ld_32x32b_x32(tbase + HALF + c * 32, ru);
+          tmem_wait_ld();
+          const int col0 = n0 + c * 32;
+          const int valid = min(32, p.N - col0);
+          if (row_ok && valid > 0) {
+            float g[32], u[32], h[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              g[i] = __uint_as_float(rg[i]);
+              u[i] = __uint_as_float(ru[i]);
+              // Round the pre-activations to bf16 first so the forward matches what the
+              // backward (which reads the stored bf16 g,u) differentiates.
+              const float gb = __bfloat162float(__float2bfloat16_rn(g[i]));
+              const float ub = __bfloat162float(__float2bfloat16_rn(u[i]));
+              h[i] = gb / (1.0f + __expf(-gb)) * ub;
+            }
+            __nv_bfloat16* d = reinterpret_cast<__nv_bfloat16*>(p.D) + (int64_t)row * p.ldd + col0;
+            store_bf16x32(d, h, valid);
+            __nv_bfloat16* gu = p.GU + (int64_t)row * p.ldgu;
+            store_bf16x32(gu + col0, g, valid);
+            store_bf16x32(gu + p.gate_up_off + col0, u, valid);
+          }
+        }
+      }
+}
+
 template <bool A_MN, bool B_MN, int BN, int STAGES>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
@@ -259,81 +340,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const int n0 = tn * out_cols;
       if (!wait_bar(&s.acc_full[acc], acc_phase, p.err, 4)) break;
       tc_fence_after();
-      const int row = m0 + q * 32 + lane;
-      const bool row_ok = row < p.M;
-      const uint32_t tbase = tmem + acc * BN + (static_cast<uint32_t>(q * 32) << 16);
-
-      if (!swiglu) {
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(tbase + c * 32, r);
-          tmem_wait_ld();
-          const int col0 = n0 + c * 32;
-          const int valid = min(32, p.N - col0);
-          if (row_ok && valid > 0) {
-            float v[32];
-#pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-            if (p.mode == EPI_STORE_BF16 || p.mode == EPI_RESID_BF16 || p.mode == EPI_ACC_BF16) {
-              __nv_bfloat16* d = reinterpret_cast<__nv_bfloat16*>(p.D) + (int64_t)row * p.ldd + col0;
-              if (p.mode != EPI_STORE_BF16) {
-                float o[32];
-                if (p.mode == EPI_RESID_BF16)
-                  load_bf16x32(p.R + (int64_t)row * p.ldr + col0, o, valid);
-                else
-                  load_bf16x32(d, o, valid);
-#pragma unroll
-                for (int i = 0; i < 32; ++i) v[i] += o[i];
-              }
-              store_bf16x32(d, v, valid);
-            } else {
-              float* d = reinterpret_cast<float*>(p.D) + (int64_t)row * p.ldd + col0;
-              float4* d4 = reinterpret_cast<float4*>(d);
-#pragma unroll
-              for (int j = 0; j < 8; ++j) {
-                if (j * 4 < valid) {
-                  float4 x = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-                  if (p.mode == EPI_ACC_F32) {
-                    float4 o = d4[j];
-                    x.x += o.x; x.y += o.y; x.z += o.z; x.w += o.w;
-                  }
-                  d4[j] = x;
-                }
-              }
-            }
-          }
-        }
-      } else {
-        constexpr int HALF = BN / 2;
-#pragma unroll 1
-        for (int c = 0; c < HALF / 32; ++c) {
-          uint32_t rg[32], ru[32];
-          tmem_ld_32x32b_x32(tbase + c * 32, rg);
-          tmem_ld_32x32b_x32(tbase + HALF + c * 32, ru);
-          tmem_wait_ld();
-          const int col0 = n0 + c * 32;
-          const int valid = min(32, p.N - col0);
-          if (row_ok && valid > 0) {
-            float g[32], u[32], h[32];
-#pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              g[i] = __uint_as_float(rg[i]);
-              u[i] = __uint_as_float(ru[i]);
-              // Round the pre-activations to bf16 first so the forward matches what the
-              // backward (which reads the stored bf16 g,u) differentiates.
-              const float gb = __bfloat162float(__float2bfloat16_rn(g[i]));
-              const float ub = __bfloat162float(__float2bfloat16_rn(u[i]));
-              h[i] = gb / (1.0f + __expf(-gb)) * ub;
-            }
-            __nv_bfloat16* d = reinterpret_cast<__nv_bfloat16*>(p.D) + (int64_t)row * p.ldd + col0;
-            store_bf16x32(d, h, valid);
-            __nv_bfloat16* gu = p.GU + (int64_t)row * p.ldgu;
-            store_bf16x32(gu + col0, g, valid);
-            store_bf16x32(gu + p.gate_up_off + col0, u, valid);
-          }
-        }
-      }
+      epilogue_tile<BN>(p, tmem + acc * BN, q, lane, m0 + q * 32 + lane, n0, swiglu);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s.acc_empty[acc]);
@@ -347,6 +354,194 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (warp == 2) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
+  }
+}
+
+
+// ------------------------------------------------------------------------------------------
+// 2-SM variant: a CTA pair (cluster of 2) computes a 256 x 256 tile with tcgen05.mma
+// cta_group::2.  Each CTA stages its own 128 rows of A and its own 128-column half of B
+// (loaded by itself, no multicast); the leader CTA issues the MMAs, whose operands come
+// from both CTAs' shared memory at the same offsets, and each CTA's TMEM receives its 128
+// accumulator rows.  Halving the B tile per CTA halves the operand bytes each SM reads per
+// MMA, which is what lets the tensor cores run at full rate.
+//   full[s]      leader only: both CTAs' TMA bytes complete on it (expect_tx = 2 stages)
+//   empty[s]     both CTAs: the leader's commit multicasts to the pair when the stage is read
+//   acc_full[a]  both CTAs: commit multicast when accumulator a is complete
+//   acc_empty[a] leader only: 4 epilogue warps of each CTA arrive (8) when a is drained
+// ------------------------------------------------------------------------------------------
+constexpr int PAIR_BN = 256;
+
+template <int STAGES>
+struct PairSmem {
+  __nv_bfloat16 a[STAGES][128 * BK];
+  __nv_bfloat16 b[STAGES][128 * BK];
+  uint64_t full[STAGES];
+  uint64_t empty[STAGES];
+  uint64_t acc_full[2];
+  uint64_t acc_empty[2];
+  uint32_t tmem_base;
+};
+
+template <bool A_MN, bool B_MN, int STAGES>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tma_a,
+                     const __grid_constant__ CUtensorMap tma_b, const Params p) {
+  using S = PairSmem<STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  S& s = *reinterpret_cast<S*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = (rank == 0);
+  const bool swiglu = (p.mode == EPI_SWIGLU_BF16);
+  const int out_cols = swiglu ? (PAIR_BN / 2) : PAIR_BN;
+  const int tiles_m = (p.M + 255) / 256;
+  const int tiles_n = (p.N + out_cols - 1) / out_cols;
+  const int num_tiles = tiles_m * tiles_n;
+  const int kblocks = (p.K + BK - 1) / BK;
+  const int pair = blockIdx.x >> 1;
+  const int npairs = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int i = 0; i < STAGES; ++i) {
+      mbar_init(&s.full[i], 1);
+      mbar_init(&s.empty[i], 1);
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s.acc_full[i], 1);
+      mbar_init(&s.acc_empty[i], 8);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 2) {
+    tmem_alloc_pair(&s.tmem_base, 512);
+    tmem_relinquish_pair();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tma_a);
+    prefetch_tmap(&tma_b);
+  }
+  tc_fence_before();
+  cluster_sync();  // barrier inits and TMEM allocations visible across the pair
+  tc_fence_after();
+  const uint32_t tmem = s.tmem_base;
+
+  if (warp == 0) {
+    // ---------------- TMA producer (both CTAs) ----------------
+    if (elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = pair; t < num_tiles && ok; t += npairs) {
+        int tm, tn;
+        tile_coords(t, tiles_m, tiles_n, p.group_m, tm, tn);
+        const int m0 = tm * 256 + static_cast<int>(rank) * 128;
+        const int n0 = tn * out_cols;
+        // K-major B rows held by this CTA (SwiGLU: leader = gate rows, peer = up rows)
+        const int brow = swiglu ? (leader ? n0 : p.gate_up_off + n0) : n0 + static_cast<int>(rank) * 128;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!wait_bar(&s.empty[stage], phase ^ 1, p.err, 11)) { ok = false; break; }
+          if (leader) mbar_arrive_expect_tx(&s.full[stage], 2 * (128 + 128) * BK * 2);
+          const uint32_t fb = mapa_shared(smem_u32(&s.full[stage]), 0);
+          const int k0 = kb * BK;
+          if (!A_MN) {
+            tma_load_2d_pair(s.a[stage], &tma_a, fb, k0, m0);
+          } else {
+            tma_load_2d_pair(s.a[stage], &tma_a, fb, m0, k0);
+            tma_load_2d_pair(s.a[stage] + 64 * BK, &tma_a, fb, m0 + 64, k0);
+          }
+          if (!B_MN) {
+            tma_load_2d_pair(s.b[stage], &tma_b, fb, k0, brow);
+          } else {
+            const int ncol = n0 + static_cast<int>(rank) * 128;
+            tma_load_2d_pair(s.b[stage], &tma_b, fb, ncol, k0);
+            tma_load_2d_pair(s.b[stage] + 64 * BK, &tma_b, fb, ncol + 64, k0);
+          }
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+      // Drain: wait until the leader's MMAs released every stage of this CTA, so no commit
+      // arrival targets this CTA's shared memory after it exits.
+      for (int i = 0; i < STAGES && ok; ++i) {
+        if (!wait_bar(&s.empty[stage], phase ^ 1, p.err, 12)) break;
+        if (++stage == STAGES) { stage = 0; phase ^= 1; }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer (leader only) ----------------
+    if (leader && elect_one()) {
+      constexpr uint32_t idesc = make_idesc_bf16(256, PAIR_BN, A_MN, B_MN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int t = pair; t < num_tiles && ok; t += npairs) {
+        if (!wait_bar(&s.acc_empty[acc], acc_phase ^ 1, p.err, 13)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem + acc * PAIR_BN;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!wait_bar(&s.full[stage], phase, p.err, 14)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(s.a[stage]);
+          const uint32_t b_base = smem_u32(s.b[stage]);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t ad = A_MN ? make_sw128_desc(a_base + kk * 2048, 64 * BK * 2, 1024)
+                                     : make_sw128_desc(a_base + kk * 32, 16, 1024);
+            const uint64_t bd = B_MN ? make_sw128_desc(b_base + kk * 2048, 64 * BK * 2, 1024)
+                                     : make_sw128_desc(b_base + kk * 32, 16, 1024);
+            mma_bf16_pair(d_tmem, ad, bd, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+          }
+          mma_commit_pair_mc(&s.empty[stage], 0x3);
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        mma_commit_pair_mc(&s.acc_full[acc], 0x3);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1;
+      }
+      // Drain: both accumulators released by both CTAs' epilogues (their remote arrivals
+      // have landed) before teardown.
+      for (int i = 0; i < 2 && ok; ++i) {
+        if (!wait_bar(&s.acc_empty[acc], acc_phase ^ 1, p.err, 15)) break;
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1;
+      }
+    }
+  } else if (warp >= EPI_WARP0) {
+    // ---------------- Epilogue (both CTAs) ----------------
+    const int q = warp - EPI_WARP0;
+    const uint32_t acc_empty_leader0 = mapa_shared(smem_u32(&s.acc_empty[0]), 0);
+    const uint32_t acc_empty_leader1 = mapa_shared(smem_u32(&s.acc_empty[1]), 0);
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = pair; t < num_tiles; t += npairs) {
+      int tm, tn;
+      tile_coords(t, tiles_m, tiles_n, p.group_m, tm, tn);
+      const int m0 = tm * 256 + static_cast<int>(rank) * 128;
+      const int n0 = tn * out_cols;
+      if (!wait_bar(&s.acc_full[acc], acc_phase, p.err, 16)) break;
+      tc_fence_after();
+      epilogue_tile<PAIR_BN>(p, tmem + acc * PAIR_BN, q, lane, m0 + q * 32 + lane, n0, swiglu);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(acc ? acc_empty_leader1 : acc_empty_leader0);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // the pair is done with each other's shared memory and TMEM
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, 512);
   }
 }
 
@@ -375,6 +570,22 @@ static void launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p
   }
   const int grid = std::max(1, std::min(num_tiles, num_sms()));
   kern<<<grid, NUM_THREADS, smem, stream>>>(ta, tb, p);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+template <bool A_MN, bool B_MN>
+static void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p,
+                        int num_tiles, cudaStream_t stream) {
+  constexpr int STAGES = 6;
+  auto kern = gemm_pair_kernel<A_MN, B_MN, STAGES>;
+  const int smem = static_cast<int>(sizeof(PairSmem<STAGES>)) + 1024;
+  static bool configured = false;
+  if (!configured) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    configured = true;
+  }
+  const int pairs = std::max(1, std::min(num_tiles, num_sms() / 2));
+  kern<<<2 * pairs, NUM_THREADS, smem, stream>>>(ta, tb, p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -445,16 +656,22 @@ void gemm_tc(const torch::Tensor& A, const torch::Tensor& B, torch::Tensor& D, b
   const c10::cuda::CUDAGuard guard(A.device());
   auto stream = at::cuda::getCurrentCUDAStream();
 
-  const int bn = choose_bn(M, N, swiglu);
+  static const int pair_mode = [] {
+    const char* e = getenv("FT_GEMM_PAIR");
+    return e ? atoi(e) : 1;
+  }();
+  const bool use_pair = pair_mode != 0 && M > 128 && (swiglu || N > 128);
+  const int bn = use_pair ? PAIR_BN : choose_bn(M, N, swiglu);
   const auto BF16 = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const int a_rows = use_pair ? 128 : BM;            // rows of A staged per CTA
+  const int b_rows = use_pair ? 128 : (swiglu ? 128 : bn);  // K-major B rows per TMA box
   CUtensorMap ta = a_mn ? make_tmap_2d(A.data_ptr(), BF16, 2, M, K, A.stride(0), 64, 64, true)
-                        : make_tmap_2d(A.data_ptr(), BF16, 2, K, M, A.stride(0), 64, BM, true);
+                        : make_tmap_2d(A.data_ptr(), BF16, 2, K, M, A.stride(0), 64, a_rows, true);
   CUtensorMap tb;
   if (b_mn)
     tb = make_tmap_2d(B.data_ptr(), BF16, 2, B.size(1), K, B.stride(0), 64, 64, true);
   else
-    tb = make_tmap_2d(B.data_ptr(), BF16, 2, K, B.size(0), B.stride(0), 64, swiglu ? 128 : bn,
-                      true);
+    tb = make_tmap_2d(B.data_ptr(), BF16, 2, K, B.size(0), B.stride(0), 64, b_rows, true);
 
   Params p;
   p.M = M; p.N = N; p.K = K;
@@ -469,6 +686,14 @@ void gemm_tc(const torch::Tensor& A, const torch::Tensor& B, torch::Tensor& D, b
   p.err = err.data_ptr<int>();
 
   const int out_cols = swiglu ? bn / 2 : bn;
+  if (use_pair) {
+    const int pair_tiles = ((M + 255) / 256) * ((N + out_cols - 1) / out_cols);
+    if (!a_mn && !b_mn) launch_pair<false, false>(ta, tb, p, pair_tiles, stream);
+    else if (!a_mn && b_mn) launch_pair<false, true>(ta, tb, p, pair_tiles, stream);
+    else if (a_mn && b_mn) launch_pair<true, true>(ta, tb, p, pair_tiles, stream);
+    else launch_pair<true, false>(ta, tb, p, pair_tiles, stream);
+    return;
+  }
   const int num_tiles = ((M + BM - 1) / BM) * ((N + out_cols - 1) / out_cols);
   if (!a_mn && !b_mn) dispatch_bn<false, false>(bn, ta, tb, p, num_tiles, stream);
   else if (!a_mn && b_mn) dispatch_bn<false, true>(bn, ta, tb, p, num_tiles, stream);
