@@ -110,6 +110,18 @@ FT_DEVICE void tma_store_2d(const CUtensorMap* map, const void* smem_src, int32_
                : "memory");
 }
 
+// Element-wise add of an fp32 smem box into global memory (the reduction happens in L2).
+FT_DEVICE void tma_reduce_add_2d(const CUtensorMap* map, const void* smem_src, int32_t x, int32_t y) {
+  asm volatile(
+      "cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3}], [%1];" ::
+          "l"(reinterpret_cast<uint64_t>(map)),
+      "r"(smem_u32(smem_src)), "r"(x), "r"(y)
+      : "memory");
+}
+FT_DEVICE void tma_store_wait_read_le1() {
+  asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+}
+
 FT_DEVICE void tma_store_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 FT_DEVICE void tma_store_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 FT_DEVICE void tma_store_wait_read() {

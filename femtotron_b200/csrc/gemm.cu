@@ -372,10 +372,52 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 // ------------------------------------------------------------------------------------------
 constexpr int PAIR_BN = 256;
 
+// fp32 epilogue through TMA: each warp moves its 32 accumulator rows 32 columns at a time
+// from TMEM into a 32x32 fp32 staging box in shared memory (128-byte swizzled rows, so the
+// row-per-lane writes hit distinct banks), then one lane issues a bulk tensor store or an
+// in-L2 reduce-add of the box into D.  The SM never reads D back, and the writes are
+// full-line, coalesced transfers.  Two staging boxes per warp alternate; a box is rewritten
+// only after the bulk copy that read it has finished reading.
+__device__ __forceinline__ void epilogue_tile_f32_tma(const Params& p, const CUtensorMap* tma_d,
+                                                      float (*box)[32 * 32], uint32_t tmem_acc,
+                                                      int q, int lane, int row0, int n0, bool add,
+                                                      int& buf) {
+  const uint32_t tbase = tmem_acc + (static_cast<uint32_t>(q * 32) << 16);
+#pragma unroll 1
+  for (int c = 0; c < PAIR_BN / 32; ++c) {
+    const int col0 = n0 + c * 32;
+    uint32_t r[32];
+    tmem_ld_32x32b_x32(tbase + c * 32, r);
+    tmem_wait_ld();
+    if (col0 >= p.N) continue;  // uniform across the warp
+    if (lane == 0) tma_store_wait_read_le1();  // box `buf` is free again
+    __syncwarp();
+    float* dst = box[buf] + lane * 32;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int pos = (j ^ (lane & 7)) * 4;
+      *reinterpret_cast<float4*>(dst + pos) = make_float4(
+          __uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]), __uint_as_float(r[4 * j + 2]),
+          __uint_as_float(r[4 * j + 3]));
+    }
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      if (add)
+        tma_reduce_add_2d(tma_d, box[buf], col0, row0);
+      else
+        tma_store_2d(tma_d, box[buf], col0, row0);
+      tma_store_commit();
+    }
+    buf ^= 1;
+  }
+}
+
 template <int STAGES>
 struct PairSmem {
   __nv_bfloat16 a[STAGES][128 * BK];
   __nv_bfloat16 b[STAGES][128 * BK];
+  float epi[4][2][32 * 32];  // per epilogue warp: two 32x32 fp32 staging boxes (SW128 layout)
   uint64_t full[STAGES];
   uint64_t empty[STAGES];
   uint64_t acc_full[2];
@@ -386,7 +428,8 @@ struct PairSmem {
 template <bool A_MN, bool B_MN, int STAGES>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tma_a,
-                     const __grid_constant__ CUtensorMap tma_b, const Params p) {
+                     const __grid_constant__ CUtensorMap tma_b,
+                     const __grid_constant__ CUtensorMap tma_d, const Params p) {
   using S = PairSmem<STAGES>;
   extern __shared__ uint8_t smem_raw[];
   S& s = *reinterpret_cast<S*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -516,6 +559,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   } else if (warp >= EPI_WARP0) {
     // ---------------- Epilogue (both CTAs) ----------------
     const int q = warp - EPI_WARP0;
+    const bool f32_out = (p.mode == EPI_ACC_F32 || p.mode == EPI_STORE_F32);
+    int epi_buf = 0;
+    if (f32_out && lane == 0) prefetch_tmap(&tma_d);
     const uint32_t acc_empty_leader0 = mapa_shared(smem_u32(&s.acc_empty[0]), 0);
     const uint32_t acc_empty_leader1 = mapa_shared(smem_u32(&s.acc_empty[1]), 0);
     int acc = 0;
@@ -527,13 +573,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       const int n0 = tn * out_cols;
       if (!wait_bar(&s.acc_full[acc], acc_phase, p.err, 16)) break;
       tc_fence_after();
-      epilogue_tile<PAIR_BN>(p, tmem + acc * PAIR_BN, q, lane, m0 + q * 32 + lane, n0, swiglu);
+      if (f32_out)
+        epilogue_tile_f32_tma(p, &tma_d, s.epi[q], tmem + acc * PAIR_BN, q, lane, m0 + q * 32, n0,
+                              p.mode == EPI_ACC_F32, epi_buf);
+      else
+        epilogue_tile<PAIR_BN>(p, tmem + acc * PAIR_BN, q, lane, m0 + q * 32 + lane, n0, swiglu);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(acc ? acc_empty_leader1 : acc_empty_leader0);
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;
     }
+    if (f32_out && lane == 0) tma_store_wait_all();  // bulk reductions done before exit
   }
 
   tc_fence_before();
@@ -574,8 +625,8 @@ static void launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p
 }
 
 template <bool A_MN, bool B_MN>
-static void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p,
-                        int num_tiles, cudaStream_t stream) {
+static void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td,
+                        const Params& p, int num_tiles, cudaStream_t stream) {
   constexpr int STAGES = 6;
   auto kern = gemm_pair_kernel<A_MN, B_MN, STAGES>;
   const int smem = static_cast<int>(sizeof(PairSmem<STAGES>)) + 1024;
@@ -585,7 +636,7 @@ static void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const Para
     configured = true;
   }
   const int pairs = std::max(1, std::min(num_tiles, num_sms() / 2));
-  kern<<<2 * pairs, NUM_THREADS, smem, stream>>>(ta, tb, p);
+  kern<<<2 * pairs, NUM_THREADS, smem, stream>>>(ta, tb, td, p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -687,11 +738,15 @@ void gemm_tc(const torch::Tensor& A, const torch::Tensor& B, torch::Tensor& D, b
 
   const int out_cols = swiglu ? bn / 2 : bn;
   if (use_pair) {
+    // fp32 output: TMA store / reduce-add map over D, 32x32 boxes with 128-byte swizzle
+    CUtensorMap td = out_f32 ? make_tmap_2d(D.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, N, M,
+                                            D.stride(0), 32, 32, true)
+                             : ta;  // unused for bf16 outputs
     const int pair_tiles = ((M + 255) / 256) * ((N + out_cols - 1) / out_cols);
-    if (!a_mn && !b_mn) launch_pair<false, false>(ta, tb, p, pair_tiles, stream);
-    else if (!a_mn && b_mn) launch_pair<false, true>(ta, tb, p, pair_tiles, stream);
-    else if (a_mn && b_mn) launch_pair<true, true>(ta, tb, p, pair_tiles, stream);
-    else launch_pair<true, false>(ta, tb, p, pair_tiles, stream);
+    if (!a_mn && !b_mn) launch_pair<false, false>(ta, tb, td, p, pair_tiles, stream);
+    else if (!a_mn && b_mn) launch_pair<false, true>(ta, tb, td, p, pair_tiles, stream);
+    else if (a_mn && b_mn) launch_pair<true, true>(ta, tb, td, p, pair_tiles, stream);
+    else launch_pair<true, false>(ta, tb, td, p, pair_tiles, stream);
     return;
   }
   const int num_tiles = ((M + BM - 1) / BM) * ((N + out_cols - 1) / out_cols);
