@@ -378,13 +378,14 @@ constexpr int PAIR_BN = 256;
 // in-L2 reduce-add of the box into D.  The SM never reads D back, and the writes are
 // full-line, coalesced transfers.  Two staging boxes per warp alternate; a box is rewritten
 // only after the bulk copy that read it has finished reading.
+template <int PBN>
 __device__ __forceinline__ void epilogue_tile_f32_tma(const Params& p, const CUtensorMap* tma_d,
                                                       float (*box)[32 * 32], uint32_t tmem_acc,
                                                       int q, int lane, int row0, int n0, bool add,
                                                       int& buf) {
   const uint32_t tbase = tmem_acc + (static_cast<uint32_t>(q * 32) << 16);
 #pragma unroll 1
-  for (int c = 0; c < PAIR_BN / 32; ++c) {
+  for (int c = 0; c < PBN / 32; ++c) {
     const int col0 = n0 + c * 32;
     uint32_t r[32];
     tmem_ld_32x32b_x32(tbase + c * 32, r);
@@ -413,10 +414,10 @@ __device__ __forceinline__ void epilogue_tile_f32_tma(const Params& p, const CUt
   }
 }
 
-template <int STAGES>
+template <int BN, int STAGES>
 struct PairSmem {
   __nv_bfloat16 a[STAGES][128 * BK];
-  __nv_bfloat16 b[STAGES][128 * BK];
+  __nv_bfloat16 b[STAGES][(BN / 2) * BK];
   float epi[4][2][32 * 32];  // per epilogue warp: two 32x32 fp32 staging boxes (SW128 layout)
   uint64_t full[STAGES];
   uint64_t empty[STAGES];
@@ -425,12 +426,12 @@ struct PairSmem {
   uint32_t tmem_base;
 };
 
-template <bool A_MN, bool B_MN, int STAGES>
+template <bool A_MN, bool B_MN, int PBN, int STAGES>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tma_a,
                      const __grid_constant__ CUtensorMap tma_b,
                      const __grid_constant__ CUtensorMap tma_d, const Params p) {
-  using S = PairSmem<STAGES>;
+  using S = PairSmem<PBN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   S& s = *reinterpret_cast<S*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
 
@@ -439,7 +440,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   const uint32_t rank = cluster_ctarank();
   const bool leader = (rank == 0);
   const bool swiglu = (p.mode == EPI_SWIGLU_BF16);
-  const int out_cols = swiglu ? (PAIR_BN / 2) : PAIR_BN;
+  constexpr int HB = PBN / 2;  // B rows (N columns) staged per CTA
+  const int out_cols = swiglu ? HB : PBN;
   const int tiles_m = (p.M + 255) / 256;
   const int tiles_n = (p.N + out_cols - 1) / out_cols;
   const int num_tiles = tiles_m * tiles_n;
@@ -485,10 +487,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         const int m0 = tm * 256 + static_cast<int>(rank) * 128;
         const int n0 = tn * out_cols;
         // K-major B rows held by this CTA (SwiGLU: leader = gate rows, peer = up rows)
-        const int brow = swiglu ? (leader ? n0 : p.gate_up_off + n0) : n0 + static_cast<int>(rank) * 128;
+        const int brow = swiglu ? (leader ? n0 : p.gate_up_off + n0) : n0 + static_cast<int>(rank) * HB;
         for (int kb = 0; kb < kblocks; ++kb) {
           if (!wait_bar(&s.empty[stage], phase ^ 1, p.err, 11)) { ok = false; break; }
-          if (leader) mbar_arrive_expect_tx(&s.full[stage], 2 * (128 + 128) * BK * 2);
+          if (leader) mbar_arrive_expect_tx(&s.full[stage], 2 * (128 + HB) * BK * 2);
           const uint32_t fb = mapa_shared(smem_u32(&s.full[stage]), 0);
           const int k0 = kb * BK;
           if (!A_MN) {
@@ -500,9 +502,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
           if (!B_MN) {
             tma_load_2d_pair(s.b[stage], &tma_b, fb, k0, brow);
           } else {
-            const int ncol = n0 + static_cast<int>(rank) * 128;
-            tma_load_2d_pair(s.b[stage], &tma_b, fb, ncol, k0);
-            tma_load_2d_pair(s.b[stage] + 64 * BK, &tma_b, fb, ncol + 64, k0);
+            const int ncol = n0 + static_cast<int>(rank) * HB;
+#pragma unroll
+            for (int j = 0; j < HB / 64; ++j)
+              tma_load_2d_pair(s.b[stage] + j * 64 * BK, &tma_b, fb, ncol + 64 * j, k0);
           }
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
@@ -517,7 +520,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   } else if (warp == 1) {
     // ---------------- MMA issuer (leader only) ----------------
     if (leader && elect_one()) {
-      constexpr uint32_t idesc = make_idesc_bf16(256, PAIR_BN, A_MN, B_MN);
+      constexpr uint32_t idesc = make_idesc_bf16(256, PBN, A_MN, B_MN);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -526,7 +529,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       for (int t = pair; t < num_tiles && ok; t += npairs) {
         if (!wait_bar(&s.acc_empty[acc], acc_phase ^ 1, p.err, 13)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t d_tmem = tmem + acc * PAIR_BN;
+        const uint32_t d_tmem = tmem + acc * PBN;
         for (int kb = 0; kb < kblocks; ++kb) {
           if (!wait_bar(&s.full[stage], phase, p.err, 14)) { ok = false; break; }
           tc_fence_after();
@@ -574,10 +577,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       if (!wait_bar(&s.acc_full[acc], acc_phase, p.err, 16)) break;
       tc_fence_after();
       if (f32_out)
-        epilogue_tile_f32_tma(p, &tma_d, s.epi[q], tmem + acc * PAIR_BN, q, lane, m0 + q * 32, n0,
-                              p.mode == EPI_ACC_F32, epi_buf);
+        epilogue_tile_f32_tma<PBN>(p, &tma_d, s.epi[q], tmem + acc * PBN, q, lane, m0 + q * 32, n0,
+                                   p.mode == EPI_ACC_F32, epi_buf);
       else
-        epilogue_tile<PAIR_BN>(p, tmem + acc * PAIR_BN, q, lane, m0 + q * 32 + lane, n0, swiglu);
+        epilogue_tile<PBN>(p, tmem + acc * PBN, q, lane, m0 + q * 32 + lane, n0, swiglu);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(acc ? acc_empty_leader1 : acc_empty_leader0);
@@ -624,12 +627,12 @@ static void launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
-template <bool A_MN, bool B_MN>
+template <bool A_MN, bool B_MN, int PBN>
 static void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td,
                         const Params& p, int num_tiles, cudaStream_t stream) {
-  constexpr int STAGES = 6;
-  auto kern = gemm_pair_kernel<A_MN, B_MN, STAGES>;
-  const int smem = static_cast<int>(sizeof(PairSmem<STAGES>)) + 1024;
+  constexpr int STAGES = PBN == 256 ? 6 : 7;
+  auto kern = gemm_pair_kernel<A_MN, B_MN, PBN, STAGES>;
+  const int smem = static_cast<int>(sizeof(PairSmem<PBN, STAGES>)) + 1024;
   static bool configured = false;
   if (!configured) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -712,10 +715,24 @@ void gemm_tc(const torch::Tensor& A, const torch::Tensor& B, torch::Tensor& D, b
     return e ? atoi(e) : 1;
   }();
   const bool use_pair = pair_mode != 0 && M > 128 && (swiglu || N > 128);
-  const int bn = use_pair ? PAIR_BN : choose_bn(M, N, swiglu);
+  // Pair tile width: 256 (best operand reuse) unless 128-wide tiles fill the last wave of
+  // CTA pairs enough better.  Cost model: waves x (tile width x k-blocks + a fixed per-tile
+  // pipeline fill/drain worth 8 k-blocks of a 256-wide tile), 5% extra for the narrow tile.
+  int pbn = 256;
+  if (use_pair && !swiglu) {
+    const long pairs = std::max(1, num_sms() / 2);
+    const long tm = (M + 255) / 256;
+    const long kb = (K + BK - 1) / BK;
+    const long c256 = (tm * ((N + 255) / 256) + pairs - 1) / pairs * (256 * kb + 2048);
+    const long c128 = (tm * ((N + 127) / 128) + pairs - 1) / pairs * (128 * kb + 2048);
+    if (c128 * 105 < c256 * 100) pbn = 128;
+    if (pair_mode == 2) pbn = 256;
+    if (pair_mode == 3) pbn = 128;
+  }
+  const int bn = use_pair ? pbn : choose_bn(M, N, swiglu);
   const auto BF16 = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   const int a_rows = use_pair ? 128 : BM;            // rows of A staged per CTA
-  const int b_rows = use_pair ? 128 : (swiglu ? 128 : bn);  // K-major B rows per TMA box
+  const int b_rows = use_pair ? bn / 2 : (swiglu ? 128 : bn);  // K-major B rows per TMA box
   CUtensorMap ta = a_mn ? make_tmap_2d(A.data_ptr(), BF16, 2, M, K, A.stride(0), 64, 64, true)
                         : make_tmap_2d(A.data_ptr(), BF16, 2, K, M, A.stride(0), 64, a_rows, true);
   CUtensorMap tb;
@@ -742,11 +759,11 @@ void gemm_tc(const torch::Tensor& A, const torch::Tensor& B, torch::Tensor& D, b
     CUtensorMap td = out_f32 ? make_tmap_2d(D.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, N, M,
                                             D.stride(0), 32, 32, true)
                              : ta;  // unused for bf16 outputs
-    const int pair_tiles = ((M + 255) / 256) * ((N + out_cols - 1) / out_cols);
-    if (!a_mn && !b_mn) launch_pair<false, false>(ta, tb, td, p, pair_tiles, stream);
-    else if (!a_mn && b_mn) launch_pair<false, true>(ta, tb, td, p, pair_tiles, stream);
-    else if (a_mn && b_mn) launch_pair<true, true>(ta, tb, td, p, pair_tiles, stream);
-    else launch_pair<true, false>(ta, tb, td, p, pair_tiles, stream);
+    const int pair_tiles = ((M + 255) / 256) * ((N + out_cols - 1) / out_cols);  // out_cols = bn (or bn/2)
+    if (!a_mn && !b_mn) (bn == 256 ? launch_pair<false, false, 256>(ta, tb, td, p, pair_tiles, stream) : launch_pair<false, false, 128>(ta, tb, td, p, pair_tiles, stream));
+    else if (!a_mn && b_mn) (bn == 256 ? launch_pair<false, true, 256>(ta, tb, td, p, pair_tiles, stream) : launch_pair<false, true, 128>(ta, tb, td, p, pair_tiles, stream));
+    else if (a_mn && b_mn) (bn == 256 ? launch_pair<true, true, 256>(ta, tb, td, p, pair_tiles, stream) : launch_pair<true, true, 128>(ta, tb, td, p, pair_tiles, stream));
+    else (bn == 256 ? launch_pair<true, false, 256>(ta, tb, td, p, pair_tiles, stream) : launch_pair<true, false, 128>(ta, tb, td, p, pair_tiles, stream));
     return;
   }
   const int num_tiles = ((M + BM - 1) / BM) * ((N + out_cols - 1) / out_cols);
