@@ -44,10 +44,12 @@ class LlamaRMSNorm(nn.Module):
         super().__init__()
         self.weight = nn.Parameter(torch.ones(hidden_size, device=device, dtype=dtype))
         self.variance_epsilon = eps
+        # set under sequence parallelism: the TP group over which tokens are sharded
+        self.sp_group = None
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         if self.weight.dtype == x.dtype and x.dtype == torch.bfloat16 or not x.is_cuda:
-            return FN.rms_norm(x, self.weight, self.variance_epsilon)
+            return FN.rms_norm(x, self.weight, self.variance_epsilon, self.sp_group)
         # non-bf16 CUDA input: PyTorch math (kept for generality; the model runs in bf16)
         xf = x.float()
         y = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + self.variance_epsilon)

@@ -65,4 +65,9 @@ def build_llama_model(model_config, parallel_ctx, *, use_pp_aware: bool = False,
         else:
             model = LlamaForTraining(model_config, parallel_ctx)
     parallelize_model(model, get_llama_parallel_plan(sequence_parallel), parallel_ctx)
+    if sequence_parallel and parallel_ctx.tp_size > 1:
+        from .layers import LlamaRMSNorm
+        for m in model.modules():
+            if isinstance(m, LlamaRMSNorm):
+                m.sp_group = parallel_ctx.tp_group
     return model

@@ -207,11 +207,15 @@ class GateUpSwiGLUFn(Function):
 
 # ------------------------------------------------------------------------------ RMSNorm
 class RMSNormFn(Function):
+    """RMSNorm; with ``sp_group`` (sequence parallelism) every rank normalises only its token
+    shard, so the weight gradient is summed over that group before it is stored."""
+
     @staticmethod
-    def forward(ctx, x, w, eps):
+    def forward(ctx, x, w, eps, sp_group=None):
         y, rstd = K.rmsnorm_fwd(x.contiguous(), w, eps)
         ctx.save_for_backward(x, w.detach(), rstd)
         ctx.param = w
+        ctx.sp_group = sp_group
         return y
 
     @staticmethod
@@ -219,13 +223,15 @@ class RMSNormFn(Function):
         x, w, rstd = ctx.saved_tensors
         dx, dw = K.rmsnorm_bwd(dy.contiguous(), x.contiguous(), w, rstd)
         if ctx.needs_input_grad[1]:
+            if ctx.sp_group is not None:
+                dist.all_reduce(dw, group=ctx.sp_group)
             write_vector_grad(ctx.param, dw)
         ctx.param = None
-        return dx, None, None
+        return dx, None, None, None
 
 
-def rms_norm(x, w, eps):
-    return RMSNormFn.apply(x, w, eps)
+def rms_norm(x, w, eps, sp_group=None):
+    return RMSNormFn.apply(x, w, eps, sp_group)
 
 
 # ------------------------------------------------------------------------------ embedding
@@ -279,8 +285,10 @@ class LMHeadCrossEntropyFn(Function):
         stats = K.xent_stats(logits, lab, vstart)
         if tp_group is not None and dist.get_world_size(tp_group) > 1:
             ws = dist.get_world_size(tp_group)
-            allst = torch.empty(ws, *stats.shape, dtype=stats.dtype, device=stats.device)
+            allst = torch.empty(ws * stats.shape[0], stats.shape[1], dtype=stats.dtype,
+                                device=stats.device)
             dist.all_gather_into_tensor(allst, stats, group=tp_group)
+            allst = allst.view(ws, *stats.shape)
             m = allst[..., 0].max(0).values
             s = (allst[..., 1] * torch.exp(allst[..., 0] - m)).sum(0)
             tgt = allst[..., 2].sum(0)

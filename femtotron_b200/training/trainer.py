@@ -49,6 +49,7 @@ class Trainer:
         self.check_finite = check_finite
         self.global_step = 0
         self.epoch = 0
+        self._resumed_mid_epoch = False
         self.history: list[dict] = []
         self._last_log_time = None
         self._last_log_step = None
@@ -61,7 +62,12 @@ class Trainer:
     def train(self):
         self.mp_manager.strategy.prepare_for_backward(self.mp_manager.groups)
         while self.global_step < self.train_config.train_steps:
-            self.dataloader.set_epoch(self.epoch)
+            if self._resumed_mid_epoch:
+                # keep the sampler offset restored from the checkpoint (set_epoch would
+                # rewind to the start of the epoch and replay samples)
+                self._resumed_mid_epoch = False
+            else:
+                self.dataloader.set_epoch(self.epoch)
             it = iter(self.dataloader)
             while self.global_step < self.train_config.train_steps:
                 try:
@@ -219,6 +225,7 @@ class Trainer:
         dl = os.path.join(ckpt_dir, f"dataloader_dp{c.dp_rank}.pt")
         if os.path.isfile(dl):
             self.dataloader.load_state_dict(torch.load(dl, weights_only=False))
+            self._resumed_mid_epoch = True
         self.global_step = meta["step"]
         self.epoch = meta["epoch"]
         if _rank() == 0:

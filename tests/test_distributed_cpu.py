@@ -1,0 +1,72 @@
+"""Distributed logic on CPU gloo ranks: topology, tensor parallelism (with and without
+sequence parallelism), ZeRO-0/1/2/3 equivalence, pipeline schedules, checkpoint resume and
+rank-failure detection.  Mirrors the reference's multi-GPU test matrix (which runs only on
+NCCL) with host-side ranks."""
+import pytest
+
+from dist_helpers import run_ranks
+import dist_workers as W
+
+
+def test_parallel_context_groups():
+    res = run_ranks(W.w_parallel_context, 4)
+    assert res[0]["coord"] == [0, 0, 0, 0, 0] and res[3]["coord"] == [1, 0, 0, 0, 1]
+    assert res[0]["tp"] == [0, 1] and res[2]["tp"] == [2, 3]
+    assert res[0]["pp"] == [0, 2] and res[1]["pp"] == [1, 3]
+    assert res[0]["next"] == 2 and res[2]["prev"] == 0 and res[2]["next"] is None
+    assert res[0]["dp_ranks"] == [0, 2]
+    assert res[0]["tp_sum"] == 1.0 and res[2]["tp_sum"] == 5.0
+
+
+@pytest.mark.parametrize("sp", [False, True])
+def test_tp_layers_match_full(sp):
+    for r in run_ranks(W.w_tp_layers, 2, sp):
+        assert all(r.values()), r
+
+
+@pytest.mark.parametrize("sp", [False, True])
+def test_tp_model_matches_single_process(sp):
+    for r in run_ranks(W.w_tp_model, 2, sp):
+        assert abs(r["loss"] - r["ref"]) < 1e-5, r
+        assert r["worst"] < 1e-4, r
+
+
+def test_zero_stages_agree():
+    curves = {s: run_ranks(W.w_zero, 2, s, False)[0] for s in (0, 1, 2, 3)}
+    base = curves[0]
+    for s, c in curves.items():
+        assert max(abs(a - b) for a, b in zip(c, base)) < 1e-4, (s, c, base)
+    assert base[-1] < base[0]
+
+
+def test_zero3_with_activation_checkpointing_agrees():
+    a = run_ranks(W.w_zero, 2, 3, True)[0]
+    b = run_ranks(W.w_zero, 2, 3, False)[0]
+    assert max(abs(x - y) for x, y in zip(a, b)) < 1e-5
+
+
+def test_grad_clipping_consistent_across_stages():
+    c0 = run_ranks(W.w_zero_clip, 2, 0)[0]
+    c3 = run_ranks(W.w_zero_clip, 2, 3)[0]
+    assert max(abs(x - y) for x, y in zip(c0, c3)) < 1e-4
+
+
+@pytest.mark.parametrize("stage", [1, 3])
+def test_checkpoint_resume_is_exact(stage, tmp_path):
+    for r in run_ranks(W.w_resume, 2, stage, str(tmp_path)):
+        assert r["full"][2:] == pytest.approx(r["resumed"], abs=1e-6), r
+
+
+@pytest.mark.parametrize("schedule", ["1f1b", "gpipe"])
+def test_pipeline_matches_single_rank(schedule):
+    res = run_ranks(W.w_pipeline, 2, schedule)
+    last = [r for r in res if r["is_last"]][0]
+    assert abs(last["loss"] - last["ref"]) < 1e-5
+    for r in res:
+        assert r["worst"] < 1e-4, r
+
+
+def test_rank_leaving_makes_peers_fail_fast():
+    res = run_ranks(W.w_rank_failure, 2, pg_timeout=5.0, timeout=120.0)
+    assert res[1] == {"left": True}
+    assert res[0]["raised"] and res[0]["elapsed"] < 60

@@ -1,0 +1,27 @@
+"""Multi-GPU (NCCL over NVLink) checks, run as torchrun child processes on 2 GPUs."""
+import json
+import os
+import subprocess
+import sys
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                    reason="needs 2 GPUs")
+def test_zero3_and_tp_sp_on_two_gpus():
+    from dist_helpers import free_port
+    cmd = ["timeout", "-k", "30", "400", sys.executable, "-m", "torch.distributed.run",
+           "--nproc-per-node", "2", "--master-addr", "127.0.0.1", "--master-port", str(free_port()),
+           os.path.join(ROOT, "tests", "mgpu", "zero_tp_check.py")]
+    out = subprocess.run(cmd, capture_output=True, text=True, timeout=460)
+    assert out.returncode == 0, out.stdout[-3000:] + out.stderr[-3000:]
+    line = [l for l in out.stdout.splitlines() if l.startswith("RESULT ")][-1]
+    r = json.loads(line[len("RESULT "):])
+    assert max(abs(a - b) for a, b in zip(r["z0"], r["z3"])) < 3e-2, r
+    assert r["z0"][-1] < r["z0"][0]
+    assert abs(r["tp1"] - r["tp2_sp"]) < 2e-2, r

@@ -1,0 +1,178 @@
+"""Pure unit tests (no process group): pipeline actions/schedules/partition/micro-batches,
+ZeRO-3 cluster layout, sampler, LR schedule, parameter groups, activation checkpointing."""
+import pytest
+import torch
+from torch import nn
+
+from femtotron_b200.parallel.pipeline_parallel import (Backward, Forward, RecvBackward, RecvForward,
+                                                       SendBackward, SendBackwardRecvForward,
+                                                       SendForward, SendForwardRecvBackward,
+                                                       gpipe_schedule, one_f_one_b_schedule,
+                                                       partition_layers, split_microbatches)
+from femtotron_b200.sharding import compute_cluster_layout
+
+
+# ------------------------------------------------------------------ actions / schedules
+def test_actions_are_frozen_hashable_and_compact():
+    a = SendForwardRecvBackward(1, 0)
+    assert repr(a) == "SFRB(1,0)" and repr(Forward(3)) == "F(3)" and repr(SendBackwardRecvForward(0, 2)) == "SBRF(0,2)"
+    assert Forward(1) == Forward(1) and hash(Forward(1)) == hash(Forward(1))
+    with pytest.raises(Exception):
+        Forward(1).mb_id = 2
+
+
+def test_gpipe_lists():
+    assert repr(gpipe_schedule(2, True, True)) == "[F(0), F(1), B(1), B(0)]"
+    assert repr(gpipe_schedule(2, True, False)) == "[F(0), SF(0), F(1), SF(1), RB(1), B(1), RB(0), B(0)]"
+    assert repr(gpipe_schedule(2, False, True)) == "[RF(0), F(0), RF(1), F(1), B(1), SB(1), B(0), SB(0)]"
+
+
+def test_1f1b_two_stage_lists():
+    assert repr(one_f_one_b_schedule(3, 2, 0)) == \
+        "[F(0), SF(0), F(1), SFRB(1,0), B(0), F(2), SFRB(2,1), B(1), RB(2), B(2)]"
+    assert repr(one_f_one_b_schedule(3, 2, 1)) == \
+        "[RF(0), F(0), B(0), SBRF(0,1), F(1), B(1), SBRF(1,2), F(2), B(2), SB(2)]"
+    assert repr(one_f_one_b_schedule(2, 1, 0)) == "[F(0), B(0), F(1), B(1)]"
+
+
+@pytest.mark.parametrize("P", [1, 2, 3, 4])
+@pytest.mark.parametrize("N", [1, 2, 3, 4, 8])
+def test_1f1b_invariants(P, N):
+    for r in range(P):
+        acts = one_f_one_b_schedule(N, P, r)
+        f = [a.mb_id for a in acts if isinstance(a, Forward)]
+        b = [a.mb_id for a in acts if isinstance(a, Backward)]
+        assert sorted(f) == list(range(N)) and sorted(b) == list(range(N))
+        for m in range(N):
+            assert acts.index(Forward(m)) < acts.index(Backward(m))
+        # in-flight forwards never exceed the warm-up depth + 1
+        live = peak = 0
+        for a in acts:
+            live += isinstance(a, Forward) - isinstance(a, Backward)
+            peak = max(peak, live)
+        assert peak <= min(P - r, N)
+        if r == 0:
+            assert not any(isinstance(a, (RecvForward, SendBackward, SendBackwardRecvForward)) for a in acts)
+        if r == P - 1:
+            assert not any(isinstance(a, (SendForward, RecvBackward, SendForwardRecvBackward)) for a in acts)
+
+
+def test_schedule_argument_validation():
+    with pytest.raises(ValueError):
+        one_f_one_b_schedule(0, 2, 0)
+    with pytest.raises(ValueError):
+        one_f_one_b_schedule(2, 2, 2)
+    with pytest.raises(ValueError):
+        gpipe_schedule(0, True, True)
+
+
+def test_partition_layers():
+    assert partition_layers(10, 4) == [range(0, 3), range(3, 6), range(6, 8), range(8, 10)]
+    assert partition_layers(8, 2, "manual", layer_counts=[5, 3]) == [range(0, 5), range(5, 8)]
+    with pytest.raises(ValueError):
+        partition_layers(2, 3)
+    with pytest.raises(ValueError):
+        partition_layers(8, 2, "manual", layer_counts=[4, 3])
+    with pytest.raises(NotImplementedError):
+        partition_layers(8, 2, "balanced")
+
+
+def test_split_microbatches_views():
+    x = torch.arange(24).view(6, 4)
+    parts = split_microbatches(x, 3)
+    assert len(parts) == 3 and parts[1].data_ptr() == x[2:4].data_ptr()
+    with pytest.raises(ValueError):
+        split_microbatches(x, 4)
+
+
+# ------------------------------------------------------------------ ZeRO-3 layout
+def test_cluster_layout_cross_boundary():
+    numels = [10, 7, 5]
+    shapes = [torch.Size([10]), torch.Size([7]), torch.Size([5])]
+    dts = [torch.bfloat16] * 3
+    lay0, shard, pad = compute_cluster_layout(numels, shapes, dts, 0, 4)
+    assert shard == 6 and pad == 2
+    assert lay0[0].has_local_view and lay0[0].local_numel == 6 and not lay0[1].has_local_view
+    lay1, _, _ = compute_cluster_layout(numels, shapes, dts, 1, 4)
+    assert lay1[0].local_offset == 0 and lay1[0].local_numel == 4
+    assert lay1[1].local_offset == 4 and lay1[1].local_numel == 2 and lay1[1].is_partially_local
+    lay3, _, _ = compute_cluster_layout(numels, shapes, dts, 3, 4)
+    assert lay3[2].local_numel == 4 and lay3[2].global_offset == 17
+    total = sum(l.local_numel for r in range(4) for l in compute_cluster_layout(numels, shapes, dts, r, 4)[0])
+    assert total == sum(numels)
+
+
+# ------------------------------------------------------------------ sampler / LR / groups
+class _Ctx:
+    def __init__(self, r, n):
+        self.dp_rank, self.dp_size = r, n
+
+
+def test_sampler_shards_and_resumes():
+    from femtotron_b200.data import DistributedSampler
+    s0, s1 = DistributedSampler(10, _Ctx(0, 2), seed=1), DistributedSampler(10, _Ctx(1, 2), seed=1)
+    a, b = list(s0), list(s1)
+    assert len(a) == len(b) == 5 and not set(a) & set(b)
+    s0.advance(2)
+    st = s0.state_dict()
+    s2 = DistributedSampler(10, _Ctx(0, 2), seed=1)
+    s2.load_state_dict(st)
+    assert list(s2) == a[2:]
+    s2.set_epoch(1)
+    assert list(s2) != a
+
+
+def test_lr_schedule_shape():
+    from femtotron_b200.training import create_lr_schedule
+    p = nn.Parameter(torch.zeros(1))
+    opt = torch.optim.SGD([p], lr=1.0)
+    sch = create_lr_schedule(opt, warmup_steps=4, total_steps=10, min_lr_ratio=0.1)
+    lrs = []
+    for _ in range(12):
+        lrs.append(opt.param_groups[0]["lr"])
+        opt.step()
+        sch.step()
+    assert lrs[0] == pytest.approx(0.25) and lrs[3] == pytest.approx(1.0)
+    assert lrs[-1] == pytest.approx(0.1) and all(a >= b for a, b in zip(lrs[3:], lrs[4:]))
+
+
+def test_param_groups_decay_rule():
+    from femtotron_b200.training import get_param_groups
+    m = nn.ModuleDict({"embed_tokens": nn.Embedding(4, 4), "lin": nn.Linear(4, 4), "norm": nn.LayerNorm(4)})
+    g = get_param_groups(m, 0.1)
+    decay = {id(p) for p in g[0]["params"]}
+    assert id(m["lin"].weight) in decay and id(m["lin"].bias) not in decay
+    assert id(m["embed_tokens"].weight) not in decay and id(m["norm"].weight) not in decay
+
+
+# ------------------------------------------------------------------ activation checkpointing
+def test_activation_checkpointing_wraps_and_keeps_names():
+    from femtotron_b200.training import (apply_activation_checkpointing, is_activation_checkpointed,
+                                         remove_activation_checkpointing)
+    from femtotron_b200.training.ckpt_policy import all_of, any_of, by_class, by_class_name, not_of
+    m = nn.Sequential(nn.Linear(4, 4), nn.ReLU(), nn.Sequential(nn.Linear(4, 4)))
+    names = set(m.state_dict().keys())
+    x = torch.randn(3, 4, requires_grad=True)
+    ref = m(x).sum()
+    ref.backward()
+    g_ref = m[0].weight.grad.clone()
+    m.zero_grad()
+    n = apply_activation_checkpointing(m, by_class(nn.Linear))
+    assert n == 2 and is_activation_checkpointed(m[0]) and is_activation_checkpointed(m[2][0])
+    assert set(m.state_dict().keys()) == names
+    m(x).sum().backward()
+    assert torch.allclose(m[0].inner_module.weight.grad, g_ref)
+    m.load_state_dict({k: v for k, v in m.state_dict().items()})
+    assert remove_activation_checkpointing(m) == 2 and not is_activation_checkpointed(m[0])
+    p = any_of(by_class_name("ReLU"), not_of(by_class(nn.Module)))
+    assert p(nn.ReLU()) and not p(nn.Linear(1, 1))
+    assert all_of(by_class(nn.Linear), by_class_name("Linear"))(nn.Linear(1, 1))
+
+
+def test_policy_from_config():
+    from femtotron_b200.training.ckpt_config import policy_from_config
+    pol = policy_from_config({"type": "any_of", "policies": [{"type": "class_name", "names": ["ReLU"]},
+                                                             {"type": "never"}]})
+    assert pol(nn.ReLU()) and not pol(nn.Linear(1, 1))
+    with pytest.raises(ValueError):
+        policy_from_config({"type": "bogus"})
