@@ -86,6 +86,11 @@ def peaks():
         return {"bf16_tflops": 1590.0, "hbm_gbs": 6650.0}
 
 
+def progress(msg: str):
+    if int(os.environ.get("RANK", "0")) == 0:
+        print(f"[bench {time.strftime('%H:%M:%S')}] {msg}", file=sys.stderr, flush=True)
+
+
 def emit(line: dict):
     if int(os.environ.get("RANK", "0")) == 0:
         print(json.dumps(line), flush=True)
@@ -159,8 +164,10 @@ def run_ours(args):
     trainer = Trainer(model, mp, sched, Null(), gsync, ctx, tc)
     mp.strategy.prepare_for_backward(mp.groups)
     it = DevIter()
-    for _ in range(args.warmup):
-        trainer.train_step(it)
+    progress("ours: model built, starting warm-up")
+    for i in range(args.warmup):
+        info = trainer.train_step(it)
+        progress(f"ours: warm-up step {i} {info['step_ms']:.0f} ms loss {info['loss']:.4f}")
     ext.check_kernel_errors(device)
     torch.cuda.synchronize()
     dist.barrier()
@@ -310,8 +317,11 @@ def run_reference(args):
         mp.strategy.prepare_for_backward(mp.groups)
         dl.set_epoch(0)
         it = iter(dl)
-        for _ in range(args.warmup):
+        progress("reference: model built, starting warm-up")
+        for i in range(args.warmup):
+            t_s = time.perf_counter()
             trainer._train_one_step(it)
+            progress(f"reference: warm-up step {i} {time.perf_counter() - t_s:.1f}s")
         torch.cuda.synchronize()
         dist.barrier()
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)

@@ -31,6 +31,17 @@ void sumsq_multi(const std::vector<torch::Tensor>& xs, const std::vector<int64_t
                  torch::Tensor& out);
 void clip_coef(const torch::Tensor& sumsq, torch::Tensor& norm_out, torch::Tensor& coef_out,
                double max_norm, double extra_scale);
+torch::Tensor symm_alloc(int64_t nbytes, int64_t device);
+torch::Tensor ipc_handle(const torch::Tensor& t);
+int64_t ipc_open(const torch::Tensor& handle, int64_t device);
+void ipc_close(int64_t ptr);
+torch::Tensor tensor_at(int64_t ptr, int64_t numel, torch::ScalarType dtype, int64_t device);
+void copy_from_ptrs(const std::vector<int64_t>& dsts, const std::vector<int64_t>& srcs,
+                    const std::vector<int64_t>& nbytes);
+void p2p_reduce_scatter(const std::vector<int64_t>& buf_ptrs, int64_t flags_local,
+                        const std::vector<int64_t>& flag_ptrs, torch::Tensor& acc, int64_t shard,
+                        int64_t rank, int64_t epoch, double scale, bool accumulate,
+                        torch::Tensor& err);
 }  // namespace ft
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -48,4 +59,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("adamw_multi", &ft::adamw_multi);
   m.def("sumsq_multi", &ft::sumsq_multi);
   m.def("clip_coef", &ft::clip_coef);
+  m.def("symm_alloc", &ft::symm_alloc);
+  m.def("ipc_handle", &ft::ipc_handle);
+  m.def("ipc_open", &ft::ipc_open);
+  m.def("ipc_close", &ft::ipc_close);
+  m.def("tensor_at", &ft::tensor_at);
+  m.def("copy_from_ptrs", &ft::copy_from_ptrs);
+  m.def("p2p_reduce_scatter", &ft::p2p_reduce_scatter);
 }

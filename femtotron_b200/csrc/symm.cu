@@ -1,0 +1,201 @@
+// Symmetric device memory across the processes of one node (one process per GPU).
+//
+// Every rank allocates a buffer of the same size with cudaMalloc (outside PyTorch's caching
+// allocator, because an IPC handle must name the base of an allocation), exports a CUDA IPC
+// handle, and opens the handles of its peers; the resulting peer pointers address the
+// peers' buffers over NVLink (NVSwitch).  On top of that this file provides:
+//   * peer copies on a stream (copy engines, no SM involvement) used by the ZeRO-3
+//     all-gather;
+//   * device flags written by the stream (cuStreamWriteValue32) so a kernel can wait for a
+//     copy without the host;
+//   * a reduce-scatter kernel that reads every peer's slice of a gradient buffer directly
+//     (P2P loads), averages in fp32 and adds into the local fp32 shard (reduce + cast +
+//     accumulate in one pass), with bounded cross-rank flag waits.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <cuda.h>
+
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+
+namespace ft {
+
+namespace {
+void check(cudaError_t e, const char* what) {
+  if (e != cudaSuccess)
+    throw std::runtime_error(std::string("femtotron_b200 symm: ") + what + ": " + cudaGetErrorString(e));
+}
+}  // namespace
+
+// Allocate `nbytes` (zeroed) with cudaMalloc and return it as a uint8 tensor that frees the
+// memory when the tensor dies.
+torch::Tensor symm_alloc(int64_t nbytes, int64_t device) {
+  const c10::cuda::CUDAGuard g(static_cast<c10::DeviceIndex>(device));
+  void* p = nullptr;
+  check(cudaMalloc(&p, static_cast<size_t>(nbytes)), "cudaMalloc");
+  check(cudaMemset(p, 0, static_cast<size_t>(nbytes)), "cudaMemset");
+  auto opts = torch::TensorOptions().dtype(torch::kUInt8).device(torch::kCUDA, device);
+  return torch::from_blob(p, {nbytes}, [](void* q) { cudaFree(q); }, opts);
+}
+
+// 64-byte CUDA IPC handle of the allocation that starts at `t`'s data pointer.
+torch::Tensor ipc_handle(const torch::Tensor& t) {
+  cudaIpcMemHandle_t h;
+  check(cudaIpcGetMemHandle(&h, t.data_ptr()), "cudaIpcGetMemHandle");
+  auto out = torch::empty({static_cast<int64_t>(sizeof(h))}, torch::kUInt8);
+  std::memcpy(out.data_ptr(), &h, sizeof(h));
+  return out;
+}
+
+// Open a peer's handle; returns the device address of its buffer in this process.
+int64_t ipc_open(const torch::Tensor& handle, int64_t device) {
+  const c10::cuda::CUDAGuard g(static_cast<c10::DeviceIndex>(device));
+  TORCH_CHECK(handle.numel() == static_cast<int64_t>(sizeof(cudaIpcMemHandle_t)));
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle.data_ptr(), sizeof(h));
+  void* p = nullptr;
+  check(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle");
+  return reinterpret_cast<int64_t>(p);
+}
+
+void ipc_close(int64_t ptr) {
+  if (ptr) cudaIpcCloseMemHandle(reinterpret_cast<void*>(ptr));
+}
+
+// A tensor view of `numel` elements of `dtype` at device address `ptr` (no ownership).
+torch::Tensor tensor_at(int64_t ptr, int64_t numel, torch::ScalarType dtype, int64_t device) {
+  auto opts = torch::TensorOptions().dtype(dtype).device(torch::kCUDA, device);
+  return torch::from_blob(reinterpret_cast<void*>(ptr), {numel}, opts);
+}
+
+// Copy engine transfers: dst[i] <- src_ptrs[i] (bytes[i] each) on the current stream.
+void copy_from_ptrs(const std::vector<int64_t>& dsts, const std::vector<int64_t>& srcs,
+                    const std::vector<int64_t>& nbytes) {
+  auto st = at::cuda::getCurrentCUDAStream();
+  for (size_t i = 0; i < dsts.size(); ++i)
+    check(cudaMemcpyAsync(reinterpret_cast<void*>(dsts[i]), reinterpret_cast<void*>(srcs[i]),
+                          static_cast<size_t>(nbytes[i]), cudaMemcpyDeviceToDevice, st),
+          "cudaMemcpyAsync");
+}
+
+// ------------------------------------------------------------------------------------------
+// P2P reduce-scatter with fused cast/scale/accumulate
+// ------------------------------------------------------------------------------------------
+// Every rank r publishes `epoch` into flags[r] of every peer when its gradient buffer is
+// complete (after the producing kernels, stream-ordered), then each rank waits (bounded) for
+// all peers' flags == epoch, reads its own slice [rank*shard, (rank+1)*shard) from all peers'
+// bf16 buffers, and computes  acc[i] (+)= scale * sum_r buf_r[rank*shard + i]  in fp32.
+struct RSArgs {
+  const __nv_bfloat16* bufs[8];  // every rank's full gradient buffer (peer addresses)
+  volatile int* flags_local;     // this rank's flag array [world]
+  int* flags_remote[8];          // flag arrays of every rank (peer addresses)
+  float* acc;                    // local fp32 shard accumulator
+  int64_t shard;
+  int world, rank, epoch, accumulate;
+  float scale;
+  int* err;
+};
+
+__device__ __forceinline__ uint64_t global_ns_() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__global__ void p2p_publish_kernel(RSArgs a) {
+  // one thread: tell every rank that this rank's buffer for `epoch` is complete
+  __threadfence_system();
+  for (int r = 0; r < a.world; ++r) {
+    asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(a.flags_remote[r] + a.rank), "r"(a.epoch)
+                 : "memory");
+  }
+}
+
+__global__ void p2p_reduce_scatter_kernel(RSArgs a) {
+  __shared__ int ok;
+  if (threadIdx.x == 0) {
+    ok = 1;
+    const uint64_t t0 = global_ns_();
+    for (int r = 0; r < a.world; ++r) {
+      while (true) {
+        int v;
+        asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(a.flags_local + r) : "memory");
+        if (v >= a.epoch) break;
+        if (global_ns_() - t0 > 5000000000ull) {  // 5 s: a peer never published
+          ok = 0;
+          atomicExch(a.err, 100 + r);
+          break;
+        }
+        __nanosleep(256);
+      }
+      if (!ok) break;
+    }
+  }
+  __syncthreads();
+  if (!ok) return;
+  const int64_t base = static_cast<int64_t>(a.rank) * a.shard;
+  const int64_t nvec = a.shard / 8;
+  for (int64_t v = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; v < nvec;
+       v += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    float s[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int r = 0; r < a.world; ++r) {
+      const uint4 q = *reinterpret_cast<const uint4*>(a.bufs[r] + base + v * 8);
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&q);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __bfloat1622float2(h[j]);
+        s[2 * j] += f.x;
+        s[2 * j + 1] += f.y;
+      }
+    }
+    float4* d = reinterpret_cast<float4*>(a.acc + v * 8);
+    float4 o0 = make_float4(s[0] * a.scale, s[1] * a.scale, s[2] * a.scale, s[3] * a.scale);
+    float4 o1 = make_float4(s[4] * a.scale, s[5] * a.scale, s[6] * a.scale, s[7] * a.scale);
+    if (a.accumulate) {
+      const float4 p0 = d[0], p1 = d[1];
+      o0.x += p0.x; o0.y += p0.y; o0.z += p0.z; o0.w += p0.w;
+      o1.x += p1.x; o1.y += p1.y; o1.z += p1.z; o1.w += p1.w;
+    }
+    d[0] = o0;
+    d[1] = o1;
+  }
+}
+
+void p2p_reduce_scatter(const std::vector<int64_t>& buf_ptrs, int64_t flags_local,
+                        const std::vector<int64_t>& flag_ptrs, torch::Tensor& acc, int64_t shard,
+                        int64_t rank, int64_t epoch, double scale, bool accumulate,
+                        torch::Tensor& err) {
+  const int world = static_cast<int>(buf_ptrs.size());
+  TORCH_CHECK(world >= 1 && world <= 8 && static_cast<int>(flag_ptrs.size()) == world);
+  TORCH_CHECK(shard % 8 == 0, "p2p_reduce_scatter: shard must be a multiple of 8");
+  TORCH_CHECK(acc.scalar_type() == at::kFloat && acc.is_contiguous() && acc.numel() >= shard);
+  RSArgs a;
+  for (int r = 0; r < world; ++r) {
+    a.bufs[r] = reinterpret_cast<const __nv_bfloat16*>(buf_ptrs[r]);
+    a.flags_remote[r] = reinterpret_cast<int*>(flag_ptrs[r]);
+  }
+  a.flags_local = reinterpret_cast<volatile int*>(flags_local);
+  a.acc = acc.data_ptr<float>();
+  a.shard = shard;
+  a.world = world;
+  a.rank = static_cast<int>(rank);
+  a.epoch = static_cast<int>(epoch);
+  a.accumulate = accumulate ? 1 : 0;
+  a.scale = static_cast<float>(scale);
+  a.err = err.data_ptr<int>();
+  auto st = at::cuda::getCurrentCUDAStream();
+  p2p_publish_kernel<<<1, 1, 0, st>>>(a);
+  int dev, sms;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t nvec = shard / 8;
+  const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((nvec + 255) / 256, sms)));
+  p2p_reduce_scatter_kernel<<<grid, 256, 0, st>>>(a);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace ft

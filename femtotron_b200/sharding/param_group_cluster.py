@@ -30,7 +30,8 @@ from .cluster_sharding_spec import compute_cluster_layout
 
 class ParamGroupCluster:
     def __init__(self, name: str, module: nn.Module, param_groups: list, dp_group,
-                 master_dtype: torch.dtype, comm_stream: torch.cuda.Stream | None = None):
+                 master_dtype: torch.dtype, comm_stream: torch.cuda.Stream | None = None,
+                 symm=None):
         if not param_groups:
             raise ValueError(f"cluster {name}: empty param_groups")
         for pg in param_groups:
@@ -55,6 +56,9 @@ class ParamGroupCluster:
         self.total_numel = sum(l.numel for l in self.layouts)
         self.padded_size = self.shard_size * self.dp_size
         self.direct = self.dp_size == 1
+        # (SymmetricHeap, byte offset): flat_param_shard lives in symmetric memory and the
+        # all-gather is a set of copy-engine pulls of every peer's shard (no SMs used)
+        self.symm = symm
 
         self.flat_param_shard = self._initialize_flat_param_shard()
         self.master = self.flat_param_shard.to(master_dtype)
@@ -80,7 +84,30 @@ class ParamGroupCluster:
         for pg, l in zip(self.param_groups, self.layouts):
             full[l.global_offset:l.global_end].copy_(pg.compute.data.reshape(-1))
         s = self.dp_rank * self.shard_size
+        if self.symm is not None:
+            heap, off = self.symm
+            shard = heap.view(off, self.shard_size, self.compute_dtype)
+            shard.copy_(full[s:s + self.shard_size])
+            return shard
         return full[s:s + self.shard_size].clone()
+
+    @staticmethod
+    def shard_numel(param_groups, dp_size: int) -> int:
+        total = sum(pg.compute.numel() for pg in param_groups)
+        return (total + dp_size - 1) // dp_size
+
+    def _gather_into(self, buf: torch.Tensor) -> None:
+        """All-gather the packed parameters into `buf` on the current stream."""
+        if self.symm is None:
+            dist.all_gather_into_tensor(buf, self.flat_param_shard, group=self.dp_group)
+            return
+        from femtotron_b200.ops.ext import native
+        heap, off = self.symm
+        nb = self.shard_size * buf.element_size()
+        base = buf.data_ptr()
+        native().copy_from_ptrs([base + r * nb for r in range(self.dp_size)],
+                                [heap.peer_ptr(r, off) for r in range(self.dp_size)],
+                                [nb] * self.dp_size)
 
     def _take_over_param_groups(self) -> None:
         for pg in self.param_groups:
@@ -106,7 +133,7 @@ class ParamGroupCluster:
         self.comm_stream.wait_stream(cur)
         with torch.cuda.stream(self.comm_stream):
             buf = torch.empty(self.padded_size, dtype=self.compute_dtype, device=self.device)
-            dist.all_gather_into_tensor(buf, self.flat_param_shard, group=self.dp_group)
+            self._gather_into(buf)
             ev = torch.cuda.Event()
             ev.record(self.comm_stream)
         self._prefetch = (buf, ev)
@@ -122,7 +149,7 @@ class ParamGroupCluster:
             buf.record_stream(cur)
         else:
             buf = torch.empty(self.padded_size, dtype=self.compute_dtype, device=self.device)
-            dist.all_gather_into_tensor(buf, self.flat_param_shard, group=self.dp_group)
+            self._gather_into(buf)
         self._full_buffer = buf
         for pg, l in zip(self.param_groups, self.layouts):
             pg.compute.data = buf[l.global_offset:l.global_end].view(l.original_shape)

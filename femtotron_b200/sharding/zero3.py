@@ -27,7 +27,7 @@ from .param_group_cluster import ParamGroupCluster
 
 
 class ZeRO3Strategy:
-    def __init__(self, dp_group, wrap_policy, prefetch: bool = True):
+    def __init__(self, dp_group, wrap_policy, prefetch: bool = True, symmetric: bool | None = None):
         self.dp_group = dp_group
         self.dp_rank = dist.get_rank(dp_group) if dp_group is not None else 0
         self.dp_size = dist.get_world_size(dp_group) if dp_group is not None else 1
@@ -37,6 +37,13 @@ class ZeRO3Strategy:
         self._hook_handles: list = []
         self._sync_enabled = True
         self.comm_stream = None
+        # parameter all-gather through copy engines from symmetric (IPC-shared) shards;
+        # default on for CUDA with dp > 1 (FT_ZERO3_SYMM=0 selects NCCL all-gather)
+        import os
+        env = os.environ.get("FT_ZERO3_SYMM")
+        self.symmetric = symmetric if symmetric is not None else (env != "0")
+        self.heap = None
+        self._barrier_t = None
 
     def make_master(self, compute: nn.Parameter, master_dtype: torch.dtype):
         master = compute.detach().clone().to(master_dtype)
@@ -59,6 +66,7 @@ class ZeRO3Strategy:
         if dev.type == "cuda" and self.dp_size > 1:
             self.comm_stream = torch.cuda.Stream(device=dev)
         names = {m: n for n, m in model.named_modules()}
+        unit_pgs = []
         for u in units:
             pgs, seen = [], set()
             for p in u.parameters():
@@ -71,10 +79,22 @@ class ZeRO3Strategy:
                 if pg.cluster is not None:
                     raise RuntimeError(f"parameter {pg.name} claimed by two units")
                 pgs.append(pg)
-            if not pgs:
-                continue
+            if pgs:
+                unit_pgs.append((u, pgs))
+        use_symm = self.symmetric and dev.type == "cuda" and self.dp_size > 1
+        offsets = []
+        if use_symm:
+            from femtotron_b200.parallel.symm import SymmetricAllocator, SymmetricHeap
+            alloc = SymmetricAllocator()
+            es = groups[0].compute.element_size()
+            for i, (u, pgs) in enumerate(unit_pgs):
+                offsets.append(alloc.reserve(f"unit{i}", ParamGroupCluster.shard_numel(pgs, self.dp_size) * es))
+            self.heap = SymmetricHeap(self.dp_group, None, alloc.size, dev)
+            self._barrier_t = torch.zeros(1, device=dev)
+        for i, (u, pgs) in enumerate(unit_pgs):
             c = ParamGroupCluster(names.get(u, type(u).__name__) or "<root>", u, pgs, self.dp_group,
-                                  master_dtype, comm_stream=self.comm_stream)
+                                  master_dtype, comm_stream=self.comm_stream,
+                                  symm=(self.heap, offsets[i]) if use_symm else None)
             self.clusters.append(c)
         for i, c in enumerate(self.clusters):
             c.index = i
@@ -156,7 +176,13 @@ class ZeRO3Strategy:
                     g.compute.copy_(g.master)
 
     def post_step(self) -> None:
-        pass
+        # Copy-engine gathers read peers' shards directly: every rank's optimizer update must
+        # be complete before any rank gathers again.  A one-element all-reduce on the compute
+        # stream is that device-side barrier.  (Peers finish reading a shard before its owner
+        # updates it because every gather of a step precedes that step's last reduce-scatter
+        # on the same communication stream, and the update waits for that reduce-scatter.)
+        if self.heap is not None:
+            dist.all_reduce(self._barrier_t, group=self.dp_group)
 
     def grads_are_dp_sharded(self) -> bool:
         return True
@@ -200,3 +226,7 @@ class ZeRO3Strategy:
             h.remove()
         self._hook_handles.clear()
         self.clusters.clear()
+        if self.heap is not None:
+            torch.cuda.synchronize()
+            self.heap.close()
+            self.heap = None
