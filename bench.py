@@ -133,7 +133,7 @@ def run_ours(args):
     from femtotron_b200.utils.clocks import ClockSampler
     from femtotron_b200.utils.dist import init_distributed, max_over_ranks
 
-    rank, world, local = init_distributed("nccl")
+    rank, world, local = init_distributed("nccl", timeout_s=int(os.environ.get("FT_PG_TIMEOUT", "600")))
     device = torch.device("cuda", local)
     cfg = model_config(args.layers)
     ctx = ParallelContext(OrderedDict(dp=world))
@@ -178,12 +178,16 @@ def run_ours(args):
         torch.cuda.synchronize()
         dist.barrier()
         start.record()
-        for _ in range(args.steps):
+        dbg_sync = os.environ.get("FT_BENCH_SYNC") == "1"
+        for i in range(args.steps):
             info = trainer._train_one_step_standard(it)
             trainer.grad_sync.sync_gradients()
             mp.step()
             sched.step()
             losses.append(info)
+            if dbg_sync:
+                torch.cuda.synchronize()
+                progress(f"ours: timed step {i} done")
         end.record()
         torch.cuda.synchronize()
         dist.barrier()

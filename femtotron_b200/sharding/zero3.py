@@ -44,6 +44,11 @@ class ZeRO3Strategy:
         self.symmetric = symmetric if symmetric is not None else (env != "0")
         self.heap = None
         self._barrier_t = None
+        # bounded host run-ahead: before issuing a gather, the host waits for the gather
+        # issued `runahead` units earlier to finish, which caps the number of in-flight
+        # full-parameter and gradient buffers (their memory is pinned by cross-stream use)
+        self.runahead = int(os.environ.get("FT_ZERO3_RUNAHEAD", "3"))
+        self._inflight: list = []
 
     def make_master(self, compute: nn.Parameter, master_dtype: torch.dtype):
         master = compute.detach().clone().to(master_dtype)
@@ -121,7 +126,17 @@ class ZeRO3Strategy:
         j = c.index + step
         return self.clusters[j] if 0 <= j < len(self.clusters) else None
 
+    def _throttle(self) -> None:
+        if self.comm_stream is None or self.runahead <= 0:
+            return
+        ev = torch.cuda.Event()
+        ev.record(torch.cuda.current_stream(self.comm_stream.device))
+        self._inflight.append(ev)
+        while len(self._inflight) > self.runahead:
+            self._inflight.pop(0).synchronize()
+
     def _pre_forward(self, c):
+        self._throttle()
         c.unshard()
         if self.prefetch_enabled and not c.in_backward:
             n = self._neighbor(c, +1)
@@ -133,6 +148,7 @@ class ZeRO3Strategy:
             c.reshard()
 
     def _pre_backward(self, c):
+        self._throttle()
         c.in_backward = True
         c.unshard()
         c.prepare_grad_buffer()
