@@ -42,6 +42,17 @@ void p2p_reduce_scatter(const std::vector<int64_t>& buf_ptrs, int64_t flags_loca
                         const std::vector<int64_t>& flag_ptrs, torch::Tensor& acc, int64_t shard,
                         int64_t rank, int64_t epoch, double scale, bool accumulate,
                         torch::Tensor& err);
+void gemm_tc_fused(const torch::Tensor& A, const torch::Tensor& B, torch::Tensor& D, bool a_mn,
+                   bool b_mn, int64_t mode,
+                   const c10::optional<torch::Tensor>& R, const c10::optional<torch::Tensor>& GU,
+                   int64_t gate_up_off, torch::Tensor& err, int64_t gate_flags, int64_t gate_op,
+                   int64_t gate_epoch, int64_t gate_off, int64_t gate_row_elems,
+                   int64_t gate_chunk_elems, const std::vector<int64_t>& scatter_ptrs,
+                   int64_t scatter_rows);
+void stream_wait_geq(int64_t addr, int64_t value);
+void stream_write(int64_t addr, int64_t value);
+void sum_partials(const torch::Tensor& parts, const c10::optional<torch::Tensor>& resid,
+                  torch::Tensor& out);
 }  // namespace ft
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -66,4 +77,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tensor_at", &ft::tensor_at);
   m.def("copy_from_ptrs", &ft::copy_from_ptrs);
   m.def("p2p_reduce_scatter", &ft::p2p_reduce_scatter);
+  m.def("gemm_tc_fused", &ft::gemm_tc_fused);
+  m.def("stream_wait_geq", &ft::stream_wait_geq);
+  m.def("stream_write", &ft::stream_write);
+  m.def("sum_partials", &ft::sum_partials);
 }

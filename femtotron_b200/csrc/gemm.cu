@@ -45,6 +45,7 @@ enum EpiMode : int {
   EPI_ACC_BF16 = 3,     // D += acc (bf16 storage, fp32 math)
   EPI_RESID_BF16 = 4,   // D = acc + R (bf16)
   EPI_SWIGLU_BF16 = 5,  // tile = [gate 128 | up 128]: D = silu(g)*u, and g,u stored to GU
+  EPI_SCATTER_BF16 = 6, // D rows stored into their owner rank's buffer (scatter_base)
 };
 
 struct Params {
@@ -59,6 +60,17 @@ struct Params {
   int gate_up_off;         // EPI_SWIGLU_BF16: first row of the up block inside B
   int group_m;
   int* err;
+  // Operand gate (fused all-gather -> GEMM): before loading a tile, the producer waits until
+  // gate_flags[c] >= gate_epoch for every chunk c the tile's operand rows touch, where row r
+  // of the gated operand lies in chunk (gate_off + r * gate_row_elems) / gate_chunk_elems.
+  const int* gate_flags;
+  int gate_op;             // 0 none, 1 gate A rows, 2 gate B rows (K-major operands only)
+  int gate_epoch;
+  int64_t gate_off, gate_row_elems, gate_chunk_elems;
+  // Scatter epilogue (fused GEMM -> reduce-scatter): row r goes to owner o = r / scatter_rows,
+  // stored at scatter_base[o] + (r - o * scatter_rows) * ldd (peer memory over NVLink).
+  __nv_bfloat16* scatter_base[8];
+  int scatter_rows;
 };
 
 __device__ __forceinline__ uint64_t global_ns() {
@@ -80,6 +92,29 @@ __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, int* er
       return false;
     }
   }
+}
+
+// Fused all-gather gate: wait (bounded) for the chunks holding operand rows [r0, r1).
+__device__ __forceinline__ bool gate_wait(const Params& p, int64_t r0, int64_t r1) {
+  if (r1 <= r0) return true;
+  const int64_t c0 = (p.gate_off + r0 * p.gate_row_elems) / p.gate_chunk_elems;
+  const int64_t c1 = (p.gate_off + (r1 - 1) * p.gate_row_elems) / p.gate_chunk_elems;
+  const uint64_t t0 = global_ns();
+  for (int64_t c = c0; c <= c1; ++c) {
+    while (true) {
+      int v;
+      asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(p.gate_flags + c) : "memory");
+      if (v - p.gate_epoch >= 0) break;
+      if (global_ns() - t0 > 4000000000ull) {
+        if (p.err) atomicExch(p.err, 40);
+        return false;
+      }
+      __nanosleep(128);
+    }
+  }
+  // data written by the copy engines is read next through the TMA (async) proxy
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+  return true;
 }
 
 // Grouped tile order: walk group_m row-tiles down a column before moving right, so one
@@ -150,9 +185,16 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t tmem_acc
             float v[32];
 #pragma unroll
             for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-            if (p.mode == EPI_STORE_BF16 || p.mode == EPI_RESID_BF16 || p.mode == EPI_ACC_BF16) {
-              __nv_bfloat16* d = reinterpret_cast<__nv_bfloat16*>(p.D) + (int64_t)row * p.ldd + col0;
-              if (p.mode != EPI_STORE_BF16) {
+            if (p.mode == EPI_STORE_BF16 || p.mode == EPI_RESID_BF16 || p.mode == EPI_ACC_BF16 ||
+                p.mode == EPI_SCATTER_BF16) {
+              __nv_bfloat16* d;
+              if (p.mode == EPI_SCATTER_BF16) {
+                const int owner = row / p.scatter_rows;
+                d = p.scatter_base[owner] + (int64_t)(row - owner * p.scatter_rows) * p.ldd + col0;
+              } else {
+                d = reinterpret_cast<__nv_bfloat16*>(p.D) + (int64_t)row * p.ldd + col0;
+              }
+              if (p.mode != EPI_STORE_BF16 && p.mode != EPI_SCATTER_BF16) {
                 float o[32];
                 if (p.mode == EPI_RESID_BF16)
                   load_bf16x32(p.R + (int64_t)row * p.ldr + col0, o, valid);
@@ -265,6 +307,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         tile_coords(t, tiles_m, tiles_n, p.group_m, tm, tn);
         const int m0 = tm * BM;
         const int n0 = tn * out_cols;
+        if (p.gate_op == 1 && !gate_wait(p, m0, min(m0 + BM, p.M))) { ok = false; break; }
+        if (p.gate_op == 2 && !gate_wait(p, n0, min(n0 + BN, p.N))) { ok = false; break; }
         for (int kb = 0; kb < kblocks; ++kb) {
           if (!wait_bar(&s.empty[stage], phase ^ 1, p.err, 1)) { ok = false; break; }
           mbar_arrive_expect_tx(&s.full[stage], (BM + BN) * BK * 2);
@@ -488,6 +532,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         const int n0 = tn * out_cols;
         // K-major B rows held by this CTA (SwiGLU: leader = gate rows, peer = up rows)
         const int brow = swiglu ? (leader ? n0 : p.gate_up_off + n0) : n0 + static_cast<int>(rank) * HB;
+        if (p.gate_op == 1 && !gate_wait(p, m0, min(m0 + 128, p.M))) { ok = false; break; }
+        if (p.gate_op == 2 && !gate_wait(p, brow, brow + HB)) { ok = false; break; }
         for (int kb = 0; kb < kblocks; ++kb) {
           if (!wait_bar(&s.empty[stage], phase ^ 1, p.err, 11)) { ok = false; break; }
           if (leader) mbar_arrive_expect_tx(&s.full[stage], 2 * (128 + HB) * BK * 2);
@@ -667,17 +713,64 @@ static int choose_bn(int M, int N, bool swiglu) {
 
 }  // namespace gemm
 
+struct GateScatter {
+  int64_t gate_flags = 0;
+  int gate_op = 0;
+  int gate_epoch = 0;
+  int64_t gate_off = 0, gate_row_elems = 1, gate_chunk_elems = 1;
+  std::vector<int64_t> scatter_ptrs;
+  int scatter_rows = 0;
+};
+
+void gemm_tc_impl(const torch::Tensor& A, const torch::Tensor& B, torch::Tensor& D, bool a_mn,
+                  bool b_mn, int64_t mode, const c10::optional<torch::Tensor>& R,
+                  const c10::optional<torch::Tensor>& GU, int64_t gate_up_off, torch::Tensor& err,
+                  const GateScatter& gs);
+
 // A: [M,K] (a_mn=false) or [K,M] (a_mn=true); B: [N,K] (b_mn=false) or [K,N] (b_mn=true).
 // D: [M,N] bf16 or fp32 per `mode`.  All operands row-major with unit inner stride.
 void gemm_tc(const torch::Tensor& A, const torch::Tensor& B, torch::Tensor& D, bool a_mn,
              bool b_mn, int64_t mode, const c10::optional<torch::Tensor>& R,
              const c10::optional<torch::Tensor>& GU, int64_t gate_up_off, torch::Tensor& err) {
+  gemm_tc_impl(A, B, D, a_mn, b_mn, mode, R, GU, gate_up_off, err, GateScatter());
+}
+
+// Fused-communication GEMM: K-major operands, optional operand gate and scatter epilogue.
+//   gate_op 1/2 gates A/B rows on int32 flags at `gate_flags` (device address);
+//   mode 6 stores row r of D into scatter_ptrs[r / scatter_rows] (row stride D.stride(0)).
+void gemm_tc_fused(const torch::Tensor& A, const torch::Tensor& B, torch::Tensor& D, bool a_mn,
+                   bool b_mn, int64_t mode,
+                   const c10::optional<torch::Tensor>& R, const c10::optional<torch::Tensor>& GU,
+                   int64_t gate_up_off, torch::Tensor& err, int64_t gate_flags, int64_t gate_op,
+                   int64_t gate_epoch, int64_t gate_off, int64_t gate_row_elems,
+                   int64_t gate_chunk_elems, const std::vector<int64_t>& scatter_ptrs,
+                   int64_t scatter_rows) {
+  GateScatter gs;
+  gs.gate_flags = gate_flags;
+  gs.gate_op = static_cast<int>(gate_op);
+  gs.gate_epoch = static_cast<int>(gate_epoch);
+  gs.gate_off = gate_off;
+  gs.gate_row_elems = std::max<int64_t>(1, gate_row_elems);
+  gs.gate_chunk_elems = std::max<int64_t>(1, gate_chunk_elems);
+  gs.scatter_ptrs = scatter_ptrs;
+  gs.scatter_rows = static_cast<int>(scatter_rows);
+  TORCH_CHECK(scatter_ptrs.size() <= 8, "gemm_tc_fused: at most 8 scatter owners");
+  if (mode == 6) TORCH_CHECK(scatter_rows > 0 && !scatter_ptrs.empty(), "gemm_tc_fused: scatter needs owners");
+  TORCH_CHECK(gs.gate_op == 0 || (gs.gate_op == 1 && !a_mn) || (gs.gate_op == 2 && !b_mn),
+              "gemm_tc_fused: only K-major operands can be gated");
+  gemm_tc_impl(A, B, D, a_mn, b_mn, mode, R, GU, gate_up_off, err, gs);
+}
+
+void gemm_tc_impl(const torch::Tensor& A, const torch::Tensor& B, torch::Tensor& D, bool a_mn,
+                  bool b_mn, int64_t mode, const c10::optional<torch::Tensor>& R,
+                  const c10::optional<torch::Tensor>& GU, int64_t gate_up_off, torch::Tensor& err,
+                  const GateScatter& gs) {
   using namespace gemm;
   TORCH_CHECK(A.is_cuda() && B.is_cuda() && D.is_cuda(), "gemm_tc: CUDA tensors required");
   TORCH_CHECK(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16,
               "gemm_tc: bf16 operands required");
   TORCH_CHECK(A.dim() == 2 && B.dim() == 2 && D.dim() == 2, "gemm_tc: 2-D operands required");
-  TORCH_CHECK(A.stride(1) == 1 && B.stride(1) == 1 && D.stride(1) == 1,
+  TORCH_CHECK(A.stride(1) == 1 && B.stride(1) == 1 && (mode == 6 || D.stride(1) == 1),
               "gemm_tc: unit inner stride required");
   const int M = a_mn ? A.size(1) : A.size(0);
   const int K = a_mn ? A.size(0) : A.size(1);
@@ -686,6 +779,7 @@ void gemm_tc(const torch::Tensor& A, const torch::Tensor& B, torch::Tensor& D, b
   const int Kb = b_mn ? B.size(0) : B.size(1);
   TORCH_CHECK(K == Kb, "gemm_tc: K mismatch ", K, " vs ", Kb);
   TORCH_CHECK(D.size(0) == M, "gemm_tc: D rows mismatch");
+  const bool scatter = (mode == 6);
   if (swiglu) {
     TORCH_CHECK(!b_mn, "gemm_tc: swiglu epilogue needs a K-major B");
     TORCH_CHECK(B.size(0) >= gate_up_off + N, "gemm_tc: swiglu B too small");
@@ -699,9 +793,10 @@ void gemm_tc(const torch::Tensor& A, const torch::Tensor& B, torch::Tensor& D, b
   TORCH_CHECK(N % 8 == 0, "gemm_tc: N must be a multiple of 8");
   const bool out_f32 = (mode == EPI_STORE_F32 || mode == EPI_ACC_F32);
   TORCH_CHECK(D.scalar_type() == (out_f32 ? at::kFloat : at::kBFloat16), "gemm_tc: D dtype");
-  TORCH_CHECK(D.stride(0) % (out_f32 ? 4 : 8) == 0 &&
-                  reinterpret_cast<uintptr_t>(D.data_ptr()) % 16 == 0,
-              "gemm_tc: D must be 16-byte aligned with an aligned row stride");
+  if (!scatter)
+    TORCH_CHECK(D.stride(0) % (out_f32 ? 4 : 8) == 0 &&
+                    reinterpret_cast<uintptr_t>(D.data_ptr()) % 16 == 0,
+                "gemm_tc: D must be 16-byte aligned with an aligned row stride");
   if (mode == EPI_RESID_BF16) {
     TORCH_CHECK(R.has_value() && R->scalar_type() == at::kBFloat16 && R->size(0) == M &&
                     R->size(1) == N && R->stride(1) == 1 && R->stride(0) % 8 == 0,
@@ -743,7 +838,8 @@ void gemm_tc(const torch::Tensor& A, const torch::Tensor& B, torch::Tensor& D, b
 
   Params p;
   p.M = M; p.N = N; p.K = K;
-  p.D = D.data_ptr(); p.ldd = D.stride(0);
+  p.D = scatter ? nullptr : D.data_ptr();
+  p.ldd = scatter ? N : D.stride(0);
   p.R = R.has_value() ? reinterpret_cast<const __nv_bfloat16*>(R->data_ptr()) : nullptr;
   p.ldr = R.has_value() ? R->stride(0) : 0;
   p.GU = GU.has_value() ? reinterpret_cast<__nv_bfloat16*>(GU->data_ptr()) : nullptr;
@@ -752,6 +848,17 @@ void gemm_tc(const torch::Tensor& A, const torch::Tensor& B, torch::Tensor& D, b
   p.gate_up_off = static_cast<int>(gate_up_off);
   p.group_m = 8;
   p.err = err.data_ptr<int>();
+  p.gate_flags = reinterpret_cast<const int*>(gs.gate_flags);
+  p.gate_op = gs.gate_op;
+  p.gate_epoch = gs.gate_epoch;
+  p.gate_off = gs.gate_off;
+  p.gate_row_elems = gs.gate_row_elems;
+  p.gate_chunk_elems = gs.gate_chunk_elems;
+  for (int i = 0; i < 8; ++i)
+    p.scatter_base[i] = i < static_cast<int>(gs.scatter_ptrs.size())
+                            ? reinterpret_cast<__nv_bfloat16*>(gs.scatter_ptrs[i])
+                            : nullptr;
+  p.scatter_rows = gs.scatter_rows;
 
   const int out_cols = swiglu ? bn / 2 : bn;
   if (use_pair) {

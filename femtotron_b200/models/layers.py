@@ -119,6 +119,18 @@ def _plain_row(m: nn.Module) -> bool:
         isinstance(m, RowParallelLinear) and m.bias is None and not m.scatter_input)
 
 
+def _sp_comm(x: torch.Tensor, group, sp: bool, world: int):
+    """The fused NVLink communication object for sequence parallelism on CUDA (else None)."""
+    if not (sp and group is not None and x.is_cuda and x.dtype == torch.bfloat16):
+        return None
+    import os
+    if os.environ.get("FT_TP_FUSED", "1") == "0":
+        return None
+    from femtotron_b200.parallel.tensor_parallel.fused import tp_fused_comm
+    rows = x.reshape(-1, x.shape[-1]).shape[0]
+    return tp_fused_comm(group, rows, x.shape[-1], x.device)
+
+
 def _enter(x: torch.Tensor, group, sp: bool) -> torch.Tensor:
     if group is None:
         return x
@@ -159,6 +171,13 @@ class LlamaAttention(nn.Module):
         nq = self.q_proj.weight.shape[0] // d
         nkv = self.k_proj.weight.shape[0] // d
         group, sp = _tp_info(self.q_proj)
+        comm = _sp_comm(x, group, sp, 0) if self._fusable() else None
+        if comm is not None and self.o_proj.weight.shape[0] == x.shape[-1]:
+            from femtotron_b200.parallel.tensor_parallel.fused import SPColumnFn, SPRowFn
+            qkv = SPColumnFn.apply(x, comm, "qkv_rope", (cos, sin, pos, nq + nkv, d, S),
+                                   self.q_proj.weight, self.k_proj.weight, self.v_proj.weight)
+            o = causal_attention(qkv, B, S, nq, nkv, d)
+            return SPRowFn.apply(o, residual, comm, self.o_proj.weight)
         if self._fusable():
             xin = _enter(x, group, sp)
             qkv = FN.QKVRopeFn.apply(xin, cos, sin, pos, nq + nkv, d, S,
@@ -212,6 +231,11 @@ class LlamaMLP(nn.Module):
 
     def forward(self, x: torch.Tensor, residual=None):
         group, sp = _tp_info(self.gate_proj)
+        comm = _sp_comm(x, group, sp, 0) if self._fusable() else None
+        if comm is not None:
+            from femtotron_b200.parallel.tensor_parallel.fused import SPColumnFn, SPRowFn
+            h = SPColumnFn.apply(x, comm, "swiglu", None, self.gate_proj.weight, self.up_proj.weight)
+            return SPRowFn.apply(h, residual, comm, self.down_proj.weight)
         if self._fusable():
             xin = _enter(x, group, sp)
             h = FN.GateUpSwiGLUFn.apply(xin, self.gate_proj.weight, self.up_proj.weight)

@@ -1,0 +1,277 @@
+"""Fused tensor-parallel communication for sequence parallelism on NVLink (one process per
+GPU): all-gather -> GEMM and GEMM -> reduce-scatter without SM-driven collectives.
+
+All-gather (AG) of a token-sharded activation x_local [Tl, H] into x_full [T = tp*Tl, H]:
+  1. the rank stages x_local in its symmetric slot and writes epoch e into every peer's
+     READY[me] flag (stream memory op, system-scope fence first);
+  2. a copy stream pulls each rank's slot (own first) with the copy engines into the local
+     x_full, each pull gated by a stream wait on READY[r] >= e and followed by a stream write
+     CHUNK[r] = e; afterwards it writes DONE[me] = e into every peer (slot may be reused);
+  3. the consuming GEMM is launched on the compute stream at once: its TMA producer waits
+     (bounded, in-kernel) on CHUNK[r] for the rows of each tile, so MMAs on local rows start
+     while peer rows are still in flight, and each remote row crosses NVLink exactly once.
+Reduce-scatter (RS) of a row-parallel GEMM's partial output over tokens:
+  1. the GEMM epilogue stores every output row straight into the receive slot of the rank
+     that owns that token (P2P stores over NVLink), then PART[me] = e is written to every
+     owner after the GEMM;
+  2. the owner's compute stream waits for PART[r] >= e from all ranks, sums the tp partials
+     of its rows in fp32 and adds the residual in one kernel, then writes CONS[me] = e into
+     every peer so the slot can be rewritten.
+Slots are double-buffered per direction; epochs increase monotonically and every rank makes
+the same sequence of calls, so stale flags are never mistaken for fresh ones.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from femtotron_b200.ops.ext import error_flag, native
+from femtotron_b200.parallel.symm import SymmetricAllocator, SymmetricHeap
+
+KINDS = ("READY", "DONE", "PART", "CONS", "CHUNK")
+NSLOTS = 2
+
+
+class TPFusedComm:
+    def __init__(self, group, rank: int, world: int, rows_local: int, cols: int, device):
+        self.group, self.rank, self.world = group, rank, world
+        self.rows_local, self.cols = rows_local, cols
+        self.device = device
+        self.slot_elems = rows_local * cols
+        sb = self.slot_elems * 2
+        a = SymmetricAllocator()
+        self.off_ag = a.reserve("ag", NSLOTS * sb)
+        self.off_rs = a.reserve("rs", NSLOTS * world * sb)
+        self.off_flags = a.reserve("flags", len(KINDS) * 64 * 4)
+        self.heap = SymmetricHeap(group, None, a.size, device)
+        self.cs = torch.cuda.Stream(device=device)
+        self.ag_epoch = 0
+        self.rs_epoch = 0
+
+    # ------------------------------------------------------------------ flags
+    def _flag_off(self, kind: str, idx: int) -> int:
+        return self.off_flags + (KINDS.index(kind) * 64 + idx) * 4
+
+    def local_flag(self, kind: str, idx: int) -> int:
+        return self.heap.peer_ptr(self.rank, self._flag_off(kind, idx))
+
+    def peer_flag(self, owner: int, kind: str, idx: int) -> int:
+        return self.heap.peer_ptr(owner, self._flag_off(kind, idx))
+
+    def fits(self, rows_local: int, cols: int) -> bool:
+        return rows_local * cols <= self.slot_elems
+
+    # ------------------------------------------------------------------ all-gather
+    def all_gather(self, x_local: torch.Tensor):
+        """Start gathering x_local [Tl, H] (bf16, contiguous); returns (x_full, epoch).  The
+        rows of rank r become valid when CHUNK[r] >= epoch (gate the consuming GEMM on it);
+        work queued on the current stream after this call also sees x_full complete."""
+        C = native()
+        Tl, H = x_local.shape
+        e = self.ag_epoch = self.ag_epoch + 1
+        s = e % NSLOTS
+        cur = torch.cuda.current_stream(self.device)
+        if e > NSLOTS:
+            for r in range(self.world):
+                C.stream_wait_geq(self.local_flag("DONE", r), e - NSLOTS)
+        slot_off = self.off_ag + s * self.slot_elems * 2
+        self.heap.view(slot_off, Tl * H, torch.bfloat16).copy_(x_local.reshape(-1))
+        for r in range(self.world):
+            C.stream_write(self.peer_flag(r, "READY", self.rank), e)
+        full = torch.empty(self.world * Tl, H, dtype=torch.bfloat16, device=self.device)
+        nb = Tl * H * 2
+        self.cs.wait_stream(cur)
+        with torch.cuda.stream(self.cs):
+            for k in range(self.world):
+                r = (self.rank + k) % self.world
+                if r != self.rank:
+                    C.stream_wait_geq(self.local_flag("READY", r), e)
+                C.copy_from_ptrs([full.data_ptr() + r * nb], [self.heap.peer_ptr(r, slot_off)], [nb])
+                C.stream_write(self.local_flag("CHUNK", r), e)
+            for r in range(self.world):
+                C.stream_write(self.peer_flag(r, "DONE", self.rank), e)
+        full.record_stream(self.cs)
+        return full, e
+
+    def gate(self, epoch: int, rows_local: int, cols: int) -> dict:
+        return dict(gate_flags=self.local_flag("CHUNK", 0), gate_op=1, gate_epoch=epoch, gate_off=0,
+                    gate_row_elems=cols, gate_chunk_elems=rows_local * cols)
+
+    def after_gated(self) -> None:
+        """Order later work on the current stream after the copy engines' pulls."""
+        torch.cuda.current_stream(self.device).wait_stream(self.cs)
+
+    # ------------------------------------------------------------------ reduce-scatter
+    def rs_begin(self, rows_local: int, cols: int):
+        """Returns (epoch, scatter pointers) for a GEMM whose row r goes to owner r // Tl."""
+        C = native()
+        e = self.rs_epoch = self.rs_epoch + 1
+        s = e % NSLOTS
+        if e > NSLOTS:
+            for r in range(self.world):
+                C.stream_wait_geq(self.local_flag("CONS", r), e - NSLOTS)
+        sb = self.slot_elems * 2
+        ptrs = [self.heap.peer_ptr(r, self.off_rs + (s * self.world + self.rank) * sb)
+                for r in range(self.world)]
+        return e, ptrs
+
+    def rs_finish(self, e: int, rows_local: int, cols: int, residual: torch.Tensor | None):
+        C = native()
+        s = e % NSLOTS
+        for r in range(self.world):
+            C.stream_write(self.peer_flag(r, "PART", self.rank), e)
+        for r in range(self.world):
+            C.stream_wait_geq(self.local_flag("PART", r), e)
+        sb = self.slot_elems * 2
+        base = self.off_rs + s * self.world * sb
+        out = torch.empty(rows_local, cols, dtype=torch.bfloat16, device=self.device)
+        if self.slot_elems == rows_local * cols:
+            parts = self.heap.view(base, self.world * rows_local * cols, torch.bfloat16).view(self.world, -1)
+        else:  # slots are larger than this call's payload: gather the used prefixes
+            parts = torch.stack([self.heap.view(base + r * sb, rows_local * cols, torch.bfloat16)
+                                 for r in range(self.world)])
+        C.sum_partials(parts, residual.reshape(-1) if residual is not None else None, out)
+        for r in range(self.world):
+            C.stream_write(self.peer_flag(r, "CONS", self.rank), e)
+        return out
+
+    def close(self):
+        torch.cuda.synchronize(self.device)
+        self.heap.close()
+
+
+def fused_gemm(a, b, out, *, a_mn=False, b_mn=False, mode="store_bf16", residual=None, gu=None,
+               gate_up_off=0, gate: dict | None = None, scatter=None):
+    """GEMM with an optional operand gate and scatter epilogue (CUDA only)."""
+    from femtotron_b200.ops.matmul import EPI_MODES
+    g = gate or {}
+    ptrs, rows = (scatter if scatter is not None else ([], 0))
+    m = 6 if scatter is not None else EPI_MODES[mode]
+    native().gemm_tc_fused(a, b, out, a_mn, b_mn, m, residual, gu, gate_up_off, error_flag(a.device),
+                           g.get("gate_flags", 0), g.get("gate_op", 0), g.get("gate_epoch", 0),
+                           g.get("gate_off", 0), g.get("gate_row_elems", 1), g.get("gate_chunk_elems", 1),
+                           list(ptrs), rows)
+    return out
+
+
+_COMMS: dict = {}
+
+
+def tp_fused_comm(group, rows_local: int, cols: int, device) -> TPFusedComm | None:
+    """The fused-communication object of a TP group, (re)created for the needed size."""
+    if group is None or not torch.cuda.is_available() or device.type != "cuda":
+        return None
+    key = (id(group), device.index)
+    c = _COMMS.get(key)
+    if c is None or not c.fits(rows_local, cols):
+        if c is not None:
+            c.close()
+        c = TPFusedComm(group, dist.get_rank(group), dist.get_world_size(group), rows_local, cols, device)
+        _COMMS[key] = c
+    return c
+
+
+# ------------------------------------------------------------------------------ autograd
+from torch.autograd import Function  # noqa: E402
+
+from femtotron_b200.ops import kernels as K  # noqa: E402
+from femtotron_b200.ops.functional import cat_rows_view, write_weight_grad  # noqa: E402
+from femtotron_b200.ops.matmul import linear_wgrad  # noqa: E402
+
+
+def _scatter_dummy(M, N, device):
+    return torch.empty(1, dtype=torch.bfloat16, device=device).expand(M, N)
+
+
+def _dgrad_rs(comm, d, W, Tl, H):
+    """dx_local [Tl, H] = reduce-scatter over tokens of d [T, N] @ W [N, H] (fused)."""
+    e, ptrs = comm.rs_begin(Tl, H)
+    fused_gemm(d, W, _scatter_dummy(d.shape[0], H, d.device), b_mn=True, scatter=(ptrs, Tl))
+    return e
+
+
+class SPColumnFn(Function):
+    """Column-parallel projection of a token-sharded input under sequence parallelism:
+    fused all-gather -> GEMM forward, fused GEMM -> reduce-scatter backward.
+    kind: "linear" | "qkv_rope" (args: cos, sin, pos, n_rot, head_dim, seq) | "swiglu"."""
+
+    @staticmethod
+    def forward(ctx, x_local, comm, kind, rope_args, *weights):
+        x2 = x_local.reshape(-1, x_local.shape[-1]).contiguous()
+        Tl, H = x2.shape
+        full, e = comm.all_gather(x2)
+        gate = comm.gate(e, Tl, H)
+        W = cat_rows_view(weights)
+        T = full.shape[0]
+        if kind == "swiglu":
+            F_ = weights[0].shape[0]
+            out = torch.empty(T, F_, dtype=x2.dtype, device=x2.device)
+            gu = torch.empty(T, 2 * F_, dtype=x2.dtype, device=x2.device)
+            fused_gemm(full, W, out, mode="swiglu", gu=gu, gate_up_off=F_, gate=gate)
+            comm.after_gated()
+            ctx.save_for_backward(full, gu, *[w.detach() for w in weights])
+        else:
+            out = torch.empty(T, W.shape[0], dtype=x2.dtype, device=x2.device)
+            fused_gemm(full, W, out, gate=gate)
+            comm.after_gated()
+            if kind == "qkv_rope":
+                cos, sin, pos, n_rot, hd, S = rope_args
+                K.rope_(out, cos, sin, n_rot, hd, S, pos=pos)
+            ctx.save_for_backward(full, *[w.detach() for w in weights])
+        ctx.comm, ctx.kind, ctx.rope_args, ctx.params = comm, kind, rope_args, weights
+        ctx.Tl, ctx.H, ctx.xshape = Tl, H, x_local.shape
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        comm, kind = ctx.comm, ctx.kind
+        if kind == "swiglu":
+            full, gu, *ws = ctx.saved_tensors
+            d = K.swiglu_bwd(dout.contiguous(), gu, ws[0].shape[0], out=gu)
+        else:
+            full, *ws = ctx.saved_tensors
+            d = dout.contiguous()
+            if kind == "qkv_rope":
+                cos, sin, pos, n_rot, hd, S = ctx.rope_args
+                d = K.rope_(d.clone(), cos, sin, n_rot, hd, S, inverse=True, pos=pos)
+        W = cat_rows_view(ws)
+        e = _dgrad_rs(comm, d, W, ctx.Tl, ctx.H)
+        write_weight_grad(ctx.params, lambda dst, acc: linear_wgrad(d, full, dst, acc))
+        dx = comm.rs_finish(e, ctx.Tl, ctx.H, None)
+        ctx.params = None
+        return (dx.view(ctx.xshape), None, None, None) + (None,) * len(ws)
+
+
+class SPRowFn(Function):
+    """Row-parallel projection under sequence parallelism: GEMM whose epilogue scatters rows
+    to their token owners, owner-side sum of the partials plus the residual (fused GEMM ->
+    reduce-scatter); backward gathers the output gradient with the fused all-gather."""
+
+    @staticmethod
+    def forward(ctx, h, residual, comm, *weights):
+        h2 = h.reshape(-1, h.shape[-1]).contiguous()
+        W = cat_rows_view(weights)
+        T, N = h2.shape[0], W.shape[0]
+        Tl = T // comm.world
+        e, ptrs = comm.rs_begin(Tl, N)
+        fused_gemm(h2, W, _scatter_dummy(T, N, h2.device), scatter=(ptrs, Tl))
+        res = residual.reshape(-1, N).contiguous() if residual is not None else None
+        out = comm.rs_finish(e, Tl, N, res)
+        ctx.save_for_backward(h2, *[w.detach() for w in weights])
+        ctx.comm, ctx.params, ctx.has_res, ctx.Tl, ctx.hshape = comm, weights, residual is not None, Tl, h.shape
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        comm = ctx.comm
+        h2, *ws = ctx.saved_tensors
+        W = cat_rows_view(ws)
+        d2 = dout.reshape(-1, dout.shape[-1]).contiguous()
+        Tl, N = d2.shape
+        dfull, e = comm.all_gather(d2)
+        dh = torch.empty(dfull.shape[0], W.shape[1], dtype=h2.dtype, device=h2.device)
+        fused_gemm(dfull, W, dh, b_mn=True, gate=comm.gate(e, Tl, N))
+        comm.after_gated()
+        write_weight_grad(ctx.params, lambda dst, acc: linear_wgrad(dfull, h2, dst, acc))
+        ctx.params = None
+        return (dh.view(ctx.hshape), dout if ctx.has_res else None, None) + (None,) * len(ws)

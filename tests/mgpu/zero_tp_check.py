@@ -60,7 +60,18 @@ def tp_loss(cfg, sd, tp, sp):
     ids = torch.randint(0, cfg.vocab_size, (2, 256), device="cuda")
     loss = m(ids, labels=ids)["loss"]
     loss.backward()
-    return loss.item()
+    # per-parameter squared gradient norms of the logical (unsharded) tensors
+    from femtotron_b200.models.parallel_plan import get_llama_parallel_plan
+    plan = get_llama_parallel_plan()
+    norms = {}
+    for n, p in m.named_parameters():
+        g = p.main_grad if getattr(p, "main_grad", None) is not None else p.grad
+        sq = g.float().pow(2).sum()
+        rule = plan.get_rule(n.rsplit(".", 1)[0]) if tp > 1 else None
+        if rule is not None and rule.parallel_type != "replicate":
+            dist.all_reduce(sq, group=ctx.tp_group)
+        norms[n] = sq.sqrt().item()
+    return loss.item(), norms
 
 
 def main():
@@ -73,9 +84,10 @@ def main():
     ctx = ParallelContext(OrderedDict(dp=dist.get_world_size()))
     z0 = train(0, ctx, cfg, sd)
     z3 = train(3, ctx, cfg, sd)
-    t1 = tp_loss(cfg, sd, 1, False)
-    t2 = tp_loss(cfg, sd, 2, True)
-    res = {"z0": z0, "z3": z3, "tp1": t1, "tp2_sp": t2}
+    t1, g1 = tp_loss(cfg, sd, 1, False)
+    t2, g2 = tp_loss(cfg, sd, 2, True)
+    worst = max(abs(g1[k] - g2[k]) / (g1[k] + 1e-12) for k in g1)
+    res = {"z0": z0, "z3": z3, "tp1": t1, "tp2_sp": t2, "grad_norm_rel_err": worst}
     if dist.get_rank() == 0:
         print("RESULT " + json.dumps(res), flush=True)
     dist.barrier()

@@ -25,3 +25,4 @@ def test_zero3_and_tp_sp_on_two_gpus():
     assert max(abs(a - b) for a, b in zip(r["z0"], r["z3"])) < 3e-2, r
     assert r["z0"][-1] < r["z0"][0]
     assert abs(r["tp1"] - r["tp2_sp"]) < 2e-2, r
+    assert r["grad_norm_rel_err"] < 5e-2, r
