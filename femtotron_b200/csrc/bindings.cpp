@@ -53,6 +53,8 @@ void stream_wait_geq(int64_t addr, int64_t value);
 void stream_write(int64_t addr, int64_t value);
 void sum_partials(const torch::Tensor& parts, const c10::optional<torch::Tensor>& resid,
                   torch::Tensor& out);
+void flash_fwd(const torch::Tensor& qkv, torch::Tensor& o, torch::Tensor& lse, int64_t B, int64_t S,
+               int64_t nq, int64_t nkv, int64_t D, torch::Tensor& err);
 }  // namespace ft
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -81,4 +83,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("stream_wait_geq", &ft::stream_wait_geq);
   m.def("stream_write", &ft::stream_write);
   m.def("sum_partials", &ft::sum_partials);
+  m.def("flash_fwd", &ft::flash_fwd);
 }

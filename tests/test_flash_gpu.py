@@ -1,0 +1,40 @@
+"""tcgen05 flash attention against fp32 causal attention (PyTorch math) of the same packed
+QKV projection: outputs, log-sum-exp and (when the backward kernel is present) gradients."""
+import math
+
+import pytest
+import torch
+
+from femtotron_b200.ops.ext import check_kernel_errors, error_flag, native
+
+pytestmark = pytest.mark.gpu
+
+
+def ref_attention(qkv, B, S, nq, nkv, d):
+    q = qkv[:, : nq * d].float().view(B, S, nq, d).transpose(1, 2)
+    k = qkv[:, nq * d:(nq + nkv) * d].float().view(B, S, nkv, d).transpose(1, 2)
+    v = qkv[:, (nq + nkv) * d:(nq + 2 * nkv) * d].float().view(B, S, nkv, d).transpose(1, 2)
+    rep = nq // nkv
+    k = k.repeat_interleave(rep, 1)
+    v = v.repeat_interleave(rep, 1)
+    s = q @ k.transpose(-1, -2) / math.sqrt(d)
+    mask = torch.ones(S, S, dtype=torch.bool, device=qkv.device).triu(1)
+    s = s.masked_fill(mask, float("-inf"))
+    lse = torch.logsumexp(s, -1)
+    o = torch.softmax(s, -1) @ v
+    return o.transpose(1, 2).reshape(B * S, nq * d), lse
+
+
+@pytest.mark.parametrize("B,S,nq,nkv,d", [(2, 256, 4, 2, 64), (1, 512, 8, 2, 128), (2, 384, 4, 4, 128)])
+def test_flash_forward_matches_reference(B, S, nq, nkv, d):
+    torch.manual_seed(0)
+    qkv = torch.randn(B * S, (nq + 2 * nkv) * d, device="cuda", dtype=torch.bfloat16)
+    o = torch.empty(B * S, nq * d, device="cuda", dtype=torch.bfloat16)
+    lse = torch.empty(B, nq, S, device="cuda", dtype=torch.float32)
+    native().flash_fwd(qkv, o, lse, B, S, nq, nkv, d, error_flag(qkv.device))
+    torch.cuda.synchronize()
+    check_kernel_errors()
+    ro, rl = ref_attention(qkv, B, S, nq, nkv, d)
+    err = ((o.float() - ro).norm() / ro.norm()).item()
+    assert err < 1e-2, err
+    assert (lse - rl).abs().max().item() < 2e-2
