@@ -103,6 +103,15 @@ FT_DEVICE void tma_load_3d(void* smem_dst, const CUtensorMap* map, uint64_t* bar
       : "memory");
 }
 
+// Untiled bulk copy global -> shared (16-byte aligned addresses, size multiple of 16).
+FT_DEVICE void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(gsrc)), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
 FT_DEVICE void tma_store_2d(const CUtensorMap* map, const void* smem_src, int32_t x, int32_t y) {
   asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%2, %3}], [%1];" ::
                    "l"(reinterpret_cast<uint64_t>(map)),

@@ -6,13 +6,17 @@
 // scores, consumed by the backward).
 //
 // One CTA computes 128 query rows of one (batch, q-head):
-//   warp 4     TMA producer: Q once, then K_j / V_j into a 2-stage ring
-//   warp 5     MMA issuer:   S_j = Q K_j^T into TMEM S[j%2]; O_j = P_j V_j into TMEM O[j%2]
-//   warps 0-3  softmax (one query row per thread): online max / exp2 / sum of S_j, P_j written
-//              to shared memory (bf16, 128-byte swizzled K-major tile), O_j accumulated into
-//              registers with the running rescale, final O / l and LSE stored.
-// TMEM: S0, S1, O0, O1 (4 x 128 fp32 columns = 512).  Causal masking only touches the
+//   warp 8     TMA producer: Q once, then K_j / V_j into a 2-stage ring
+//   warp 9     MMA issuer:   S_j = Q K_j^T into TMEM S[j%2]; O += P_j V_j into TMEM O
+//   warps 0-7  softmax: two warps per TMEM lane quadrant (32 query rows), each owning 64 of
+//              the 128 key columns; they exchange the row max through shared memory, keep
+//              P_j relative to a lazily updated max (O in TMEM is rescaled only when the max
+//              grows by more than 2^8), write P_j to shared memory (bf16, 128-byte swizzled
+//              K-major tile) and finally store O / l and the LSE.
+// TMEM: S0, S1 (2 x 128 fp32 columns), O (D columns).  Causal masking only touches the
 // diagonal block; blocks past the diagonal are skipped.  Every mbarrier wait is bounded.
+//
+// Reference: the reference calls torch SDPA (femtotron/model/llama_partial_model.py:70).
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -93,8 +97,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   // heaviest (latest) query blocks first for causal load balance
-  const int qb = p.nqb - 1 - static_cast<int>(blockIdx.x);
-  const int bh = blockIdx.y;
+  // (every head's first wave holds the longest rows, so the short ones fill the tail)
+  const int qb = p.nqb - 1 - static_cast<int>(blockIdx.y);
+  const int bh = blockIdx.x;
   const int b = bh / p.nq, h = bh % p.nq;
   const int g = h / (p.nq / p.nkv);
   const int row0 = b * p.S + qb * BQ;          // first token row of this query block
@@ -359,7 +364,7 @@ void flash_fwd(const torch::Tensor& qkv, torch::Tensor& o, torch::Tensor& lse, i
   p.scale_log2 = static_cast<float>(1.0 / std::sqrt(static_cast<double>(D))) * kLog2e;
   p.nqb = S / 128;
   p.err = err.data_ptr<int>();
-  dim3 grid(S / 128, B * nq);
+  dim3 grid(B * nq, S / 128);
   auto st = at::cuda::getCurrentCUDAStream();
   if (D == 128) {
     const int smem = sizeof(Smem<128>) + 1024;

@@ -8,11 +8,15 @@ from __future__ import annotations
 
 import torch
 
-from .ext import has_native, native
+from .ext import error_flag, has_native, native
 
 
-def flash_available(head_dim: int) -> bool:
-    return has_native() and hasattr(native(), "flash_fwd") and head_dim in (64, 128)
+def flash_available(head_dim: int, seq_len: int = 128) -> bool:
+    """True when the native kernels cover this shape (head size 64/128, S a multiple of 128)."""
+    if not has_native() or head_dim not in (64, 128) or seq_len % 128 != 0:
+        return False
+    m = native()
+    return hasattr(m, "flash_fwd") and hasattr(m, "flash_bwd")
 
 
 class FlashAttnFn(torch.autograd.Function):
@@ -20,7 +24,7 @@ class FlashAttnFn(torch.autograd.Function):
     def forward(ctx, qkv, B, S, nq, nkv, d):
         o = torch.empty(B * S, nq * d, dtype=qkv.dtype, device=qkv.device)
         lse = torch.empty(B, nq, S, dtype=torch.float32, device=qkv.device)
-        native().flash_fwd(qkv, o, lse, B, S, nq, nkv, d)
+        native().flash_fwd(qkv, o, lse, B, S, nq, nkv, d, error_flag(qkv.device))
         ctx.save_for_backward(qkv, o, lse)
         ctx.meta = (B, S, nq, nkv, d)
         return o
@@ -30,7 +34,8 @@ class FlashAttnFn(torch.autograd.Function):
         qkv, o, lse = ctx.saved_tensors
         B, S, nq, nkv, d = ctx.meta
         dqkv = torch.empty_like(qkv)
-        native().flash_bwd(qkv, o, do.contiguous(), lse, dqkv, B, S, nq, nkv, d)
+        native().flash_bwd(qkv, o, do.contiguous(), lse, dqkv, B, S, nq, nkv, d,
+                          error_flag(qkv.device))
         return dqkv, None, None, None, None, None
 
 

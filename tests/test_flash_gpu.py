@@ -38,3 +38,42 @@ def test_flash_forward_matches_reference(B, S, nq, nkv, d):
     err = ((o.float() - ro).norm() / ro.norm()).item()
     assert err < 1e-2, err
     assert (lse - rl).abs().max().item() < 2e-2
+
+
+@pytest.mark.parametrize("B,S,nq,nkv,d", [(2, 256, 4, 2, 64), (1, 512, 8, 2, 128), (2, 384, 4, 4, 128)])
+def test_flash_backward_matches_reference(B, S, nq, nkv, d):
+    torch.manual_seed(1)
+    qkv = torch.randn(B * S, (nq + 2 * nkv) * d, device="cuda", dtype=torch.bfloat16)
+    o = torch.empty(B * S, nq * d, device="cuda", dtype=torch.bfloat16)
+    lse = torch.empty(B, nq, S, device="cuda", dtype=torch.float32)
+    native().flash_fwd(qkv, o, lse, B, S, nq, nkv, d, error_flag(qkv.device))
+    do = torch.randn(B * S, nq * d, device="cuda", dtype=torch.bfloat16)
+    dqkv = torch.empty_like(qkv)
+    native().flash_bwd(qkv, o, do, lse, dqkv, B, S, nq, nkv, d, error_flag(qkv.device))
+    torch.cuda.synchronize()
+    check_kernel_errors()
+    x = qkv.float().requires_grad_(True)
+    ro, _ = ref_attention(x, B, S, nq, nkv, d)
+    ro.backward(do.float())
+    ref = x.grad
+    for name, sl in (("dq", slice(0, nq * d)), ("dk", slice(nq * d, (nq + nkv) * d)),
+                     ("dv", slice((nq + nkv) * d, (nq + 2 * nkv) * d))):
+        got, want = dqkv[:, sl].float(), ref[:, sl]
+        rel = ((got - want).norm() / want.norm()).item()
+        assert rel < 2e-2, (name, rel)
+
+
+def test_flash_attention_autograd_function():
+    from femtotron_b200.ops.attention import flash_attention, flash_available
+    B, S, nq, nkv, d = 1, 256, 4, 2, 128
+    assert flash_available(d, S)
+    torch.manual_seed(2)
+    qkv = torch.randn(B * S, (nq + 2 * nkv) * d, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    o = flash_attention(qkv, B, S, nq, nkv, d)
+    g = torch.randn_like(o)
+    o.backward(g)
+    x = qkv.detach().float().requires_grad_(True)
+    ro, _ = ref_attention(x, B, S, nq, nkv, d)
+    ro.backward(g.float())
+    assert ((o.float() - ro).norm() / ro.norm()).item() < 1e-2
+    assert ((qkv.grad.float() - x.grad).norm() / x.grad.norm()).item() < 2e-2
