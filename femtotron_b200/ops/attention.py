@@ -8,7 +8,12 @@ from __future__ import annotations
 
 import torch
 
+import os
+
 from .ext import error_flag, has_native, native
+
+# FT_ATTN=sdpa routes attention to torch SDPA (for A/B measurements against the library)
+USE_NATIVE = os.environ.get("FT_ATTN", "native") != "sdpa"
 
 
 def flash_available(head_dim: int, seq_len: int = 128) -> bool:

@@ -1,0 +1,214 @@
+"""Kernel micro-benchmark and roofline report for the native sm_100a kernels.
+
+    python -m femtotron_b200.utils.kbench all            # every op, Llama-3-8B shapes
+    python -m femtotron_b200.utils.kbench gemm_qkv --iters 20
+    python -m femtotron_b200.utils.kbench flash_fwd --compare   # also time the torch library op
+
+Each op is timed with CUDA events on the launching stream after warm-up, with a synchronize
+on both sides; inputs are larger than L2 (126 MB) where the op is memory-bound, otherwise an
+L2-sized buffer is rewritten between iterations.  The report gives achieved TFLOP/s or GB/s and
+the fraction of the measured peaks (MEASURED_PEAKS.json at the repository root when present,
+else the pool's fallback of 6.65 TB/s and 1.59 PFLOP/s).  One JSON line per op.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+
+import torch
+import torch.nn.functional as F
+
+from femtotron_b200.ops import kernels as K
+from femtotron_b200.ops.ext import check_kernel_errors, error_flag, native
+from femtotron_b200.ops.matmul import gemm
+
+# Llama-3-8B, one micro-batch of 4096 tokens
+T, H, FF, V, NQ, NKV, D = 4096, 4096, 14336, 128256, 32, 8, 128
+
+
+def peaks() -> dict:
+    p = os.path.join(os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))),
+                     "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return {"tflops": float(d["bf16_tflops"]), "gbs": float(d["hbm_gbs"]), "src": "measured"}
+    except (OSError, KeyError, ValueError):
+        return {"tflops": 1590.0, "gbs": 6650.0, "src": "fallback"}
+
+
+_FLUSH = None
+
+
+def flush_l2():
+    global _FLUSH
+    if _FLUSH is None:
+        _FLUSH = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    _FLUSH.zero_()
+
+
+def timed(fn, iters: int, warmup: int = 3, flush: bool = False) -> float:
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    total = 0.0
+    for _ in range(iters):
+        if flush:
+            flush_l2()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        fn()
+        e.record()
+        torch.cuda.synchronize()
+        total += s.elapsed_time(e)
+    return total / iters
+
+
+def bf(*shape):
+    return torch.randn(*shape, device="cuda", dtype=torch.bfloat16)
+
+
+def op_gemm(name, M, N, K_, a_mn=False, b_mn=False, mode="store_bf16"):
+    a = bf(K_, M) if a_mn else bf(M, K_)
+    b = bf(K_, N) if b_mn else bf(N, K_)
+    out = torch.empty(M, N, device="cuda",
+                      dtype=torch.float32 if mode.endswith("f32") else torch.bfloat16)
+
+    def run():
+        gemm(a, b, out, a_mn=a_mn, b_mn=b_mn, mode=mode)
+
+    def lib():
+        aa = a.t() if a_mn else a
+        bb = b if b_mn else b.t()
+        torch.mm(aa, bb)
+    return {"kind": "flops", "flops": 2.0 * M * N * K_, "run": run, "lib": lib, "name": name}
+
+
+def op_flash(name, bwd: bool):
+    B, S = 1, T
+    qkv = bf(B * S, (NQ + 2 * NKV) * D)
+    o = torch.empty(B * S, NQ * D, device="cuda", dtype=torch.bfloat16)
+    lse = torch.empty(B, NQ, S, device="cuda", dtype=torch.float32)
+    err = error_flag(qkv.device)
+    fl = 4.0 * B * NQ * S * S * D / 2
+    q = qkv[:, : NQ * D].view(B, S, NQ, D).transpose(1, 2)
+    k = qkv[:, NQ * D:(NQ + NKV) * D].view(B, S, NKV, D).transpose(1, 2)
+    v = qkv[:, (NQ + NKV) * D:].view(B, S, NKV, D).transpose(1, 2)
+    if not bwd:
+        def run():
+            native().flash_fwd(qkv, o, lse, B, S, NQ, NKV, D, err)
+
+        def lib():
+            F.scaled_dot_product_attention(q, k, v, is_causal=True, enable_gqa=True)
+        return {"kind": "flops", "flops": fl, "run": run, "lib": lib, "name": name}
+    native().flash_fwd(qkv, o, lse, B, S, NQ, NKV, D, err)
+    do = bf(B * S, NQ * D)
+    dqkv = torch.empty_like(qkv)
+    qq, kk, vv = [x.detach().clone().requires_grad_(True) for x in (q, k, v)]
+    out = F.scaled_dot_product_attention(qq, kk, vv, is_causal=True, enable_gqa=True)
+    go = torch.randn_like(out)
+
+    def run():
+        native().flash_bwd(qkv, o, do, lse, dqkv, B, S, NQ, NKV, D, err)
+
+    def lib():
+        torch.autograd.grad(out, (qq, kk, vv), go, retain_graph=True)
+    return {"kind": "flops", "flops": 2.5 * fl, "run": run, "lib": lib, "name": name}
+
+
+def op_rmsnorm(name, bwd: bool):
+    x, w = bf(4 * T, H), torch.ones(H, device="cuda", dtype=torch.bfloat16)
+    if not bwd:
+        def run():
+            K.rmsnorm_fwd(x, w, 1e-5)
+        return {"kind": "bytes", "bytes": 2.0 * x.numel() * 2 + 4 * x.shape[0], "run": run, "name": name}
+    y, rstd = K.rmsnorm_fwd(x, w, 1e-5)
+    dy = bf(4 * T, H)
+
+    def run():
+        K.rmsnorm_bwd(dy, x, w, rstd)
+    return {"kind": "bytes", "bytes": 3.0 * x.numel() * 2, "run": run, "name": name}
+
+
+def op_swiglu(name):
+    gu = bf(4 * T, 2 * FF)
+
+    def run():
+        K.swiglu_fwd(gu, FF)
+    return {"kind": "bytes", "bytes": gu.numel() * 2 * 1.5, "run": run, "name": name}
+
+
+def op_adamw(name):
+    n = 218 * 1000 * 1000  # one Llama-3-8B decoder layer
+    p, m, v, g = (torch.randn(n, device="cuda") for _ in range(4))
+    out = torch.empty(n, device="cuda", dtype=torch.bfloat16)
+
+    def run():
+        K.adamw_multi([p], [m], [v], [g], [out], [0.1], lr=1e-4, beta1=0.9, beta2=0.95, eps=1e-8,
+                      step=10)
+    # read p, m, v, g (fp32), write p, m, v (fp32) + bf16 copy
+    return {"kind": "bytes", "bytes": n * (4 * 4 + 3 * 4 + 2), "run": run, "name": name}
+
+
+def op_xent(name):
+    logits = bf(T, V)
+    labels = torch.randint(0, V, (T,), device="cuda")
+
+    def run():
+        K.xent_stats(logits, labels, 0)
+    return {"kind": "bytes", "bytes": logits.numel() * 2, "run": run, "name": name}
+
+
+OPS = {
+    "gemm_qkv": lambda: op_gemm("gemm_qkv", T, (NQ + 2 * NKV) * D, H),
+    "gemm_o": lambda: op_gemm("gemm_o", T, H, NQ * D),
+    "gemm_gateup": lambda: op_gemm("gemm_gateup", T, 2 * FF, H),
+    "gemm_down": lambda: op_gemm("gemm_down", T, H, FF),
+    "gemm_lmhead": lambda: op_gemm("gemm_lmhead", T, V, H),
+    "gemm_dgrad_gateup": lambda: op_gemm("gemm_dgrad_gateup", T, H, 2 * FF, b_mn=True),
+    "gemm_wgrad_gateup": lambda: op_gemm("gemm_wgrad_gateup", 2 * FF, H, T, a_mn=True, b_mn=True,
+                                         mode="acc_f32"),
+    "flash_fwd": lambda: op_flash("flash_fwd", False),
+    "flash_bwd": lambda: op_flash("flash_bwd", True),
+    "rmsnorm_fwd": lambda: op_rmsnorm("rmsnorm_fwd", False),
+    "rmsnorm_bwd": lambda: op_rmsnorm("rmsnorm_bwd", True),
+    "swiglu_fwd": lambda: op_swiglu("swiglu_fwd"),
+    "adamw": lambda: op_adamw("adamw"),
+    "xent_stats": lambda: op_xent("xent_stats"),
+}
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("op", choices=sorted(OPS) + ["all"])
+    ap.add_argument("--iters", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--compare", action="store_true", help="also time the torch library op")
+    args = ap.parse_args(argv)
+    pk = peaks()
+    names = sorted(OPS) if args.op == "all" else [args.op]
+    for n in names:
+        spec = OPS[n]()
+        flush = spec["kind"] == "flops"  # memory-bound ops already use inputs larger than L2
+        ms = timed(spec["run"], args.iters, args.warmup, flush=flush)
+        check_kernel_errors()
+        rec = {"op": n, "ms": round(ms, 4)}
+        if spec["kind"] == "flops":
+            tf = spec["flops"] / ms / 1e9
+            rec.update(tflops=round(tf, 1), frac_of_peak=round(tf / pk["tflops"], 3))
+            if args.compare and "lib" in spec:
+                lms = timed(spec["lib"], args.iters, args.warmup, flush=True)
+                rec.update(lib_ms=round(lms, 4), lib_tflops=round(spec["flops"] / lms / 1e9, 1))
+        else:
+            gbs = spec["bytes"] / ms / 1e6
+            rec.update(gbs=round(gbs, 1), frac_of_peak=round(gbs / pk["gbs"], 3))
+        rec["peak_src"] = pk["src"]
+        print(json.dumps(rec), flush=True)
+        del spec
+        torch.cuda.empty_cache()
+
+
+if __name__ == "__main__":
+    main()
