@@ -179,12 +179,18 @@ def run_ours(args):
         dist.barrier()
         start.record()
         dbg_sync = os.environ.get("FT_BENCH_SYNC") == "1"
+        from femtotron_b200.utils.comm_timing import TIMER
+        TIMER.collect()
+        comm_tot: dict = {}
         for i in range(args.steps):
             info = trainer._train_one_step_standard(it)
             trainer.grad_sync.sync_gradients()
             mp.step()
             sched.step()
             losses.append(info)
+            if TIMER.enabled:  # diagnostic mode: syncs on the step's wait events
+                for k, v in TIMER.collect().items():
+                    comm_tot[k] = comm_tot.get(k, 0.0) + v
             if dbg_sync:
                 torch.cuda.synchronize()
                 progress(f"ours: timed step {i} done")
@@ -226,6 +232,10 @@ def run_ours(args):
 
     pk = peaks()
     mfu = value * flops_per_token(cfg, S) / (world * pk["bf16_tflops"] * 1e12)
+    exposed = None
+    if comm_tot:
+        # compute-stream time blocked on communication, per step, max over ranks
+        exposed = {k: round(max_over_ranks(v) / args.steps, 2) for k, v in sorted(comm_tot.items())}
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 2),
@@ -244,6 +254,8 @@ def run_ours(args):
     }
     if e2e is not None:
         line["e2e"] = e2e
+    if exposed is not None:
+        line["exposed_comm_ms_per_step"] = exposed
     emit(line)
     dist.barrier()
     dist.destroy_process_group()

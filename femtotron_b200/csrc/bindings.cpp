@@ -38,6 +38,9 @@ void ipc_close(int64_t ptr);
 torch::Tensor tensor_at(int64_t ptr, int64_t numel, torch::ScalarType dtype, int64_t device);
 void copy_from_ptrs(const std::vector<int64_t>& dsts, const std::vector<int64_t>& srcs,
                     const std::vector<int64_t>& nbytes);
+void reduce_slices_f32(const std::vector<int64_t>& src_ptrs, torch::Tensor& acc, int64_t n,
+                       double scale, bool accumulate);
+void p2p_publish(const std::vector<int64_t>& flag_ptrs, int64_t rank, int64_t epoch);
 void p2p_reduce_scatter(const std::vector<int64_t>& buf_ptrs, int64_t flags_local,
                         const std::vector<int64_t>& flag_ptrs, torch::Tensor& acc, int64_t shard,
                         int64_t rank, int64_t epoch, double scale, bool accumulate,
@@ -82,6 +85,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tensor_at", &ft::tensor_at);
   m.def("copy_from_ptrs", &ft::copy_from_ptrs);
   m.def("p2p_reduce_scatter", &ft::p2p_reduce_scatter);
+  m.def("p2p_publish", &ft::p2p_publish);
+  m.def("reduce_slices_f32", &ft::reduce_slices_f32);
   m.def("gemm_tc_fused", &ft::gemm_tc_fused);
   m.def("stream_wait_geq", &ft::stream_wait_geq);
   m.def("stream_write", &ft::stream_write);

@@ -85,17 +85,22 @@ void copy_from_ptrs(const std::vector<int64_t>& dsts, const std::vector<int64_t>
 // ------------------------------------------------------------------------------------------
 // P2P reduce-scatter with fused cast/scale/accumulate
 // ------------------------------------------------------------------------------------------
-// Every rank r publishes `epoch` into flags[r] of every peer when its gradient buffer is
-// complete (after the producing kernels, stream-ordered), then each rank waits (bounded) for
-// all peers' flags == epoch, reads its own slice [rank*shard, (rank+1)*shard) from all peers'
-// bf16 buffers, and computes  acc[i] (+)= scale * sum_r buf_r[rank*shard + i]  in fp32.
+// Protocol (one flag array of `world` int32 per buffer, in symmetric memory):
+//   p2p_publish (compute stream, after the kernels that wrote this rank's bf16 buffer):
+//       flags_of_rank_r[this rank] = epoch for every r (release, system scope);
+//   p2p_reduce_scatter (communication stream): wait (bounded) until every peer's flag in the
+//       local array is >= epoch, then read slice [rank*shard, (rank+1)*shard) of every peer's
+//       buffer over NVLink and write  acc[i] (+)= scale * sum_r buf_r[rank*shard + i]  in fp32.
+// Peers may reuse their buffers only after every rank's reduction has finished; the caller
+// provides that ordering (a device-side barrier between steps).
 struct RSArgs {
   const __nv_bfloat16* bufs[8];  // every rank's full gradient buffer (peer addresses)
   volatile int* flags_local;     // this rank's flag array [world]
   int* flags_remote[8];          // flag arrays of every rank (peer addresses)
   float* acc;                    // local fp32 shard accumulator
   int64_t shard;
-  int world, rank, epoch, accumulate;
+  int64_t base;                  // element offset of the reduced slice inside every buffer
+  int world, rank, epoch, accumulate, wait;
   float scale;
   int* err;
 };
@@ -115,36 +120,44 @@ __global__ void p2p_publish_kernel(RSArgs a) {
   }
 }
 
-__global__ void p2p_reduce_scatter_kernel(RSArgs a) {
-  __shared__ int ok;
-  if (threadIdx.x == 0) {
-    ok = 1;
-    const uint64_t t0 = global_ns_();
-    for (int r = 0; r < a.world; ++r) {
-      while (true) {
-        int v;
-        asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(a.flags_local + r) : "memory");
-        if (v >= a.epoch) break;
-        if (global_ns_() - t0 > 5000000000ull) {  // 5 s: a peer never published
-          ok = 0;
-          atomicExch(a.err, 100 + r);
-          break;
-        }
-        __nanosleep(256);
+// Bounded wait (20 s: a peer that is that late has failed) for all peers' flags >= epoch.
+__device__ __forceinline__ bool wait_peers(const RSArgs& a) {
+  const uint64_t t0 = global_ns_();
+  for (int r = 0; r < a.world; ++r) {
+    while (true) {
+      int v;
+      asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(a.flags_local + r) : "memory");
+      if (v - a.epoch >= 0) break;
+      if (global_ns_() - t0 > 20000000000ull) {
+        atomicExch(a.err, 100 + r);
+        return false;
       }
-      if (!ok) break;
+      __nanosleep(512);
     }
   }
-  __syncthreads();
-  if (!ok) return;
-  const int64_t base = static_cast<int64_t>(a.rank) * a.shard;
+  return true;
+}
+
+__global__ void p2p_reduce_scatter_kernel(RSArgs a) {
+  if (a.wait) {
+    __shared__ int ok;
+    if (threadIdx.x == 0) ok = wait_peers(a) ? 1 : 0;
+    __syncthreads();
+    if (!ok) return;
+  }
+  const int64_t base = a.base;
   const int64_t nvec = a.shard / 8;
   for (int64_t v = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; v < nvec;
        v += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     float s[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    for (int r = 0; r < a.world; ++r) {
-      const uint4 q = *reinterpret_cast<const uint4*>(a.bufs[r] + base + v * 8);
-      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&q);
+    uint4 q[8];
+#pragma unroll
+    for (int r = 0; r < 8; ++r)
+      if (r < a.world) q[r] = *reinterpret_cast<const uint4*>(a.bufs[r] + base + v * 8);
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      if (r >= a.world) break;
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&q[r]);
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const float2 f = __bfloat1622float2(h[j]);
@@ -165,36 +178,84 @@ __global__ void p2p_reduce_scatter_kernel(RSArgs a) {
   }
 }
 
+namespace {
+RSArgs make_rs_args(const std::vector<int64_t>& buf_ptrs, const std::vector<int64_t>& flag_ptrs,
+                    int64_t rank, int64_t epoch) {
+  const int world = static_cast<int>(flag_ptrs.size());
+  TORCH_CHECK(world >= 1 && world <= 8, "p2p: 1..8 ranks");
+  TORCH_CHECK(buf_ptrs.empty() || static_cast<int>(buf_ptrs.size()) == world);
+  RSArgs a{};
+  for (int r = 0; r < world; ++r) {
+    if (!buf_ptrs.empty()) a.bufs[r] = reinterpret_cast<const __nv_bfloat16*>(buf_ptrs[r]);
+    a.flags_remote[r] = reinterpret_cast<int*>(flag_ptrs[r]);
+  }
+  a.world = world;
+  a.rank = static_cast<int>(rank);
+  a.epoch = static_cast<int>(epoch);
+  return a;
+}
+}  // namespace
+
+// Publish this rank's buffer for `epoch` to every rank (flag_ptrs[r] = rank r's flag array).
+void p2p_publish(const std::vector<int64_t>& flag_ptrs, int64_t rank, int64_t epoch) {
+  RSArgs a = make_rs_args({}, flag_ptrs, rank, epoch);
+  p2p_publish_kernel<<<1, 1, 0, at::cuda::getCurrentCUDAStream()>>>(a);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 void p2p_reduce_scatter(const std::vector<int64_t>& buf_ptrs, int64_t flags_local,
                         const std::vector<int64_t>& flag_ptrs, torch::Tensor& acc, int64_t shard,
                         int64_t rank, int64_t epoch, double scale, bool accumulate,
                         torch::Tensor& err) {
-  const int world = static_cast<int>(buf_ptrs.size());
-  TORCH_CHECK(world >= 1 && world <= 8 && static_cast<int>(flag_ptrs.size()) == world);
-  TORCH_CHECK(shard % 8 == 0, "p2p_reduce_scatter: shard must be a multiple of 8");
   TORCH_CHECK(acc.scalar_type() == at::kFloat && acc.is_contiguous() && acc.numel() >= shard);
-  RSArgs a;
-  for (int r = 0; r < world; ++r) {
-    a.bufs[r] = reinterpret_cast<const __nv_bfloat16*>(buf_ptrs[r]);
-    a.flags_remote[r] = reinterpret_cast<int*>(flag_ptrs[r]);
-  }
+  TORCH_CHECK(shard % 8 == 0, "p2p_reduce_scatter: shard must be a multiple of 8 elements");
+  RSArgs a = make_rs_args(buf_ptrs, flag_ptrs, rank, epoch);
+  for (int r = 0; r < a.world; ++r)
+    TORCH_CHECK((reinterpret_cast<uintptr_t>(a.bufs[r]) & 15) == 0,
+                "p2p_reduce_scatter: buffers must be 16-byte aligned");
   a.flags_local = reinterpret_cast<volatile int*>(flags_local);
   a.acc = acc.data_ptr<float>();
   a.shard = shard;
-  a.world = world;
-  a.rank = static_cast<int>(rank);
-  a.epoch = static_cast<int>(epoch);
+  a.base = rank * shard;
+  a.wait = 1;
   a.accumulate = accumulate ? 1 : 0;
   a.scale = static_cast<float>(scale);
   a.err = err.data_ptr<int>();
-  auto st = at::cuda::getCurrentCUDAStream();
-  p2p_publish_kernel<<<1, 1, 0, st>>>(a);
   int dev, sms;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int64_t nvec = shard / 8;
   const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((nvec + 255) / 256, sms)));
-  p2p_reduce_scatter_kernel<<<grid, 256, 0, st>>>(a);
+  p2p_reduce_scatter_kernel<<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(a);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Local reduction of `world` bf16 slices (already in this GPU's memory, e.g. pulled from the
+// peers by copy engines) into the fp32 shard: acc (+)= scale * sum_r src_r.  No waits.
+void reduce_slices_f32(const std::vector<int64_t>& src_ptrs, torch::Tensor& acc, int64_t n,
+                       double scale, bool accumulate) {
+  TORCH_CHECK(acc.scalar_type() == at::kFloat && acc.is_contiguous() && acc.numel() >= n);
+  TORCH_CHECK(n % 8 == 0, "reduce_slices_f32: n must be a multiple of 8");
+  const int world = static_cast<int>(src_ptrs.size());
+  TORCH_CHECK(world >= 1 && world <= 8);
+  RSArgs a{};
+  for (int r = 0; r < world; ++r) {
+    a.bufs[r] = reinterpret_cast<const __nv_bfloat16*>(src_ptrs[r]);
+    TORCH_CHECK((src_ptrs[r] & 15) == 0, "reduce_slices_f32: 16-byte aligned sources");
+  }
+  a.world = world;
+  a.acc = acc.data_ptr<float>();
+  a.shard = n;
+  a.base = 0;
+  a.wait = 0;
+  a.accumulate = accumulate ? 1 : 0;
+  a.scale = static_cast<float>(scale);
+  int dev, sms;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t nvec = n / 8;
+  const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((nvec + 255) / 256, 2 * sms)));
+  p2p_reduce_scatter_kernel<<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(a);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

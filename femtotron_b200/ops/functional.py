@@ -68,10 +68,24 @@ def _grad_target(p: torch.Tensor):
     return p.grad, True
 
 
+def grad_ready(p: torch.Tensor) -> None:
+    """Tell the owner of parameter p (a sharding strategy) that this backward's contribution
+    to its gradient has been enqueued, so a reduction can start early."""
+    cb = getattr(p, "_ft_grad_ready", None)
+    if cb is not None:
+        cb()
+
+
 def write_weight_grad(params, compute):
     """Route `compute(dst2d, accumulate)` (dst2d = [sum rows, cols]) to the gradient sinks of
     the 2-D weights `params`, used together as one stacked operand."""
     params = list(params)
+    _write_weight_grad(params, compute)
+    for p in params:
+        grad_ready(p)
+
+
+def _write_weight_grad(params, compute):
     targets = [_grad_target(p) for p in params]
     dsts = [t.view(p.shape) for (t, _), p in zip(targets, params)]
     accs = [a for _, a in targets]
@@ -101,6 +115,7 @@ def write_vector_grad(p: torch.Tensor, g32: torch.Tensor):
         dst.add_(g.to(dst.dtype))
     else:
         dst.copy_(g)
+    grad_ready(p)
 
 
 def _as2d(x: torch.Tensor) -> torch.Tensor:
@@ -262,6 +277,7 @@ class EmbeddingFn(Function):
                 native().embed_bwd(ids.reshape(-1).contiguous(),
                                    dout.reshape(-1, dout.shape[-1]).contiguous(),
                                    mg.view(weight.shape), int(ctx.vstart))
+                grad_ready(weight)
             else:
                 write_vector_grad(weight, K.embed_bwd(ids, dout, weight.shape[0], ctx.vstart))
         return None, None, None

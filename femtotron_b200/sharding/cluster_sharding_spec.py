@@ -40,12 +40,15 @@ class ClusterShardingSpec:
         return self.has_local_view and self.local_numel < self.numel
 
 
-def compute_cluster_layout(param_numels, param_shapes, param_dtypes, dp_rank: int, dp_size: int):
-    """Returns (layouts, shard_size, pad_size)."""
+def compute_cluster_layout(param_numels, param_shapes, param_dtypes, dp_rank: int, dp_size: int,
+                           align: int = 1):
+    """Returns (layouts, shard_size, pad_size).  ``align`` rounds the shard size up to a
+    multiple of that many elements (vectorised peer reductions need 16-byte slices)."""
     if not (len(param_numels) == len(param_shapes) == len(param_dtypes)):
         raise ValueError("param_numels, param_shapes and param_dtypes differ in length")
     total = sum(param_numels)
-    padded = ((total + dp_size - 1) // dp_size) * dp_size
+    unit = dp_size * max(1, int(align))
+    padded = ((total + unit - 1) // unit) * unit
     shard = padded // dp_size
     lo, hi = dp_rank * shard, dp_rank * shard + shard
     layouts = []

@@ -16,8 +16,16 @@ Two modes:
     straight into the optimizer's gradient: no gather, no scatter, no copies.
   * dp_size > 1: ``unshard`` all-gathers the packed parameters (optionally prefetched on a
     communication stream), ``reshard`` drops them; during a unit's backward the gradients
-    go to a transient bf16 buffer that ``reduce_scatter_grads`` reduce-scatters (AVG) on the
-    communication stream and adds into flat_grad_shard.
+    go to a bf16 buffer that ``reduce_scatter_grads`` reduces (AVG) into flat_grad_shard on
+    the communication stream.
+
+With a symmetric heap (CUDA, dp > 1) the packed parameter shard and the bf16 gradient buffer
+live in IPC-shared memory: the all-gather is copy-engine pulls of every peer's shard, and the
+reduce-scatter is the native P2P kernel (publish an epoch flag to every peer after the unit's
+backward; a kernel on the communication stream waits for all peers' flags, reads its slice of
+every peer's buffer over NVLink and writes the fp32 shard, averaging and accumulating in the
+same pass).  The reference does both with NCCL collectives
+(femtotron/sharding/param_group_cluster.py:248-252, :321-324).
 """
 from __future__ import annotations
 
@@ -31,7 +39,7 @@ from .cluster_sharding_spec import compute_cluster_layout
 class ParamGroupCluster:
     def __init__(self, name: str, module: nn.Module, param_groups: list, dp_group,
                  master_dtype: torch.dtype, comm_stream: torch.cuda.Stream | None = None,
-                 symm=None):
+                 symm=None, symm_grad=None):
         if not param_groups:
             raise ValueError(f"cluster {name}: empty param_groups")
         for pg in param_groups:
@@ -52,13 +60,23 @@ class ParamGroupCluster:
         self.comm_stream = comm_stream
         self.layouts, self.shard_size, self.pad_size = compute_cluster_layout(
             [pg.compute.numel() for pg in param_groups], [pg.compute.shape for pg in param_groups],
-            [pg.compute.dtype for pg in param_groups], self.dp_rank, self.dp_size)
+            [pg.compute.dtype for pg in param_groups], self.dp_rank, self.dp_size,
+            align=self.SYMM_ALIGN if symm is not None else 1)
         self.total_numel = sum(l.numel for l in self.layouts)
         self.padded_size = self.shard_size * self.dp_size
         self.direct = self.dp_size == 1
         # (SymmetricHeap, byte offset): flat_param_shard lives in symmetric memory and the
         # all-gather is a set of copy-engine pulls of every peer's shard (no SMs used)
         self.symm = symm
+        # (gradient buffer byte offset, flag array byte offset) in the same heap: P2P
+        # reduce-scatter instead of NCCL
+        self.symm_grad = symm_grad if symm is not None else None
+        self._rs_epoch = 0
+        # reduce-scatter flavour over the symmetric gradient buffer: "ce" (copy engines pull
+        # the peers' slices after a stream-side flag wait, then a local reduce kernel) or
+        # "p2p" (one kernel that waits for the flags and loads the peers' slices itself)
+        self.rs_mode = "ce"
+        self.rs_stream = None
 
         self.flat_param_shard = self._initialize_flat_param_shard()
         self.master = self.flat_param_shard.to(master_dtype)
@@ -91,10 +109,14 @@ class ParamGroupCluster:
             return shard
         return full[s:s + self.shard_size].clone()
 
+    # shard size granularity (elements) when the unit lives in symmetric memory
+    SYMM_ALIGN = 64
+
     @staticmethod
-    def shard_numel(param_groups, dp_size: int) -> int:
+    def shard_numel(param_groups, dp_size: int, align: int = 1) -> int:
         total = sum(pg.compute.numel() for pg in param_groups)
-        return (total + dp_size - 1) // dp_size
+        unit = dp_size * max(1, align)
+        return (total + unit - 1) // unit * max(1, align)
 
     def _gather_into(self, buf: torch.Tensor) -> None:
         """All-gather the packed parameters into `buf` on the current stream."""
@@ -141,15 +163,18 @@ class ParamGroupCluster:
     def unshard(self) -> None:
         if self.direct or self._full_buffer is not None:
             return
+        from femtotron_b200.utils.comm_timing import TIMER
         if self._prefetch is not None:
             buf, ev = self._prefetch
             self._prefetch = None
             cur = torch.cuda.current_stream(self.device)
-            cur.wait_event(ev)
+            with TIMER.wait("param_gather"):
+                cur.wait_event(ev)
             buf.record_stream(cur)
         else:
             buf = torch.empty(self.padded_size, dtype=self.compute_dtype, device=self.device)
-            self._gather_into(buf)
+            with TIMER.wait("param_gather_inline"):
+                self._gather_into(buf)
         self._full_buffer = buf
         for pg, l in zip(self.param_groups, self.layouts):
             pg.compute.data = buf[l.global_offset:l.global_end].view(l.original_shape)
@@ -167,7 +192,14 @@ class ParamGroupCluster:
         (dp > 1) for the upcoming backward of this unit."""
         if self.direct or self._grad_buffer is not None:
             return
-        gb = torch.zeros(self.padded_size, dtype=self.compute_dtype, device=self.device)
+        if self.symm_grad is not None:
+            # persistent symmetric buffer: every peer finished reading it in the previous
+            # step (the optimizer step is followed by a device-side barrier)
+            heap = self.symm[0]
+            gb = heap.view(self.symm_grad[0], self.padded_size, self.compute_dtype)
+            gb.zero_()
+        else:
+            gb = torch.zeros(self.padded_size, dtype=self.compute_dtype, device=self.device)
         self._grad_buffer = gb
         for pg, l in zip(self.param_groups, self.layouts):
             pg.compute.main_grad = gb[l.global_offset:l.global_end].view(l.original_shape)
@@ -184,6 +216,9 @@ class ParamGroupCluster:
             pg.compute.main_grad = None
         fresh = self._grad_fresh
         self._grad_fresh = False
+        if self.symm_grad is not None:
+            self._p2p_reduce_scatter(accumulate=not fresh)
+            return
         use_stream = self.comm_stream is not None and self.device.type == "cuda"
         if use_stream:
             cur = torch.cuda.current_stream(self.device)
@@ -200,6 +235,37 @@ class ParamGroupCluster:
                 self.flat_grad_shard.copy_(tmp)
             else:
                 self.flat_grad_shard.add_(tmp.to(torch.float32))
+
+    def _p2p_reduce_scatter(self, accumulate: bool) -> None:
+        from femtotron_b200.ops.ext import error_flag, native
+        C = native()
+        heap = self.symm[0]
+        goff, foff = self.symm_grad
+        self._rs_epoch += 1
+        ep = self._rs_epoch
+        R, rank = self.dp_size, self.dp_rank
+        flags = [heap.peer_ptr(r, foff) for r in range(R)]
+        cur = torch.cuda.current_stream(self.device)
+        C.p2p_publish(flags, rank, ep)          # after this unit's backward kernels
+        st = self.rs_stream or self.comm_stream
+        st.wait_stream(cur)
+        with torch.cuda.stream(st):
+            if self.rs_mode == "p2p":
+                C.p2p_reduce_scatter([heap.peer_ptr(r, goff) for r in range(R)], flags[rank], flags,
+                                     self.flat_grad_shard, self.shard_size, rank, ep, 1.0 / R,
+                                     accumulate, error_flag(self.device))
+                return
+            nb = self.shard_size * 2
+            for r in range(R):                  # peers' flags, waited in the stream (no SMs)
+                if r != rank:
+                    C.stream_wait_geq(flags[rank] + 4 * r, ep)
+            stage = torch.empty(R - 1, self.shard_size, dtype=self.compute_dtype, device=self.device)
+            peers = [r for r in range(R) if r != rank]
+            C.copy_from_ptrs([stage[i].data_ptr() for i in range(R - 1)],
+                             [heap.peer_ptr(r, goff) + rank * nb for r in peers], [nb] * (R - 1))
+            own = heap.peer_ptr(rank, goff) + rank * nb
+            C.reduce_slices_f32([own] + [stage[i].data_ptr() for i in range(R - 1)],
+                                self.flat_grad_shard, self.shard_size, 1.0 / R, accumulate)
 
     def populate_master_grad(self) -> None:
         """Point the optimizer's views at the reduced fp32 gradient (no copy)."""

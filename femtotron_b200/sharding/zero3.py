@@ -17,6 +17,7 @@ With dp_size == 1 the clusters run in direct mode (no hooks, no copies).
 """
 from __future__ import annotations
 
+import os
 from contextlib import contextmanager
 
 import torch
@@ -37,9 +38,9 @@ class ZeRO3Strategy:
         self._hook_handles: list = []
         self._sync_enabled = True
         self.comm_stream = None
-        # parameter all-gather through copy engines from symmetric (IPC-shared) shards;
-        # default on for CUDA with dp > 1 (FT_ZERO3_SYMM=0 selects NCCL all-gather)
-        import os
+        # all-gather through copy engines from symmetric (IPC-shared) shards and a reduce-scatter
+        # over symmetric gradient buffers; default on for CUDA with dp > 1 (FT_ZERO3_SYMM=0
+        # selects NCCL for both; FT_ZERO3_RS=ce|p2p|nccl picks the reduce-scatter flavour)
         env = os.environ.get("FT_ZERO3_SYMM")
         self.symmetric = symmetric if symmetric is not None else (env != "0")
         self.heap = None
@@ -49,6 +50,9 @@ class ZeRO3Strategy:
         # full-parameter and gradient buffers (their memory is pinned by cross-stream use)
         self.runahead = int(os.environ.get("FT_ZERO3_RUNAHEAD", "3"))
         self._inflight: list = []
+        self.ar_stream = None
+        self.rs_stream = None
+        self._early_reduced: set[int] = set()
 
     def make_master(self, compute: nn.Parameter, master_dtype: torch.dtype):
         master = compute.detach().clone().to(master_dtype)
@@ -87,30 +91,69 @@ class ZeRO3Strategy:
             if pgs:
                 unit_pgs.append((u, pgs))
         use_symm = self.symmetric and dev.type == "cuda" and self.dp_size > 1
-        offsets = []
+        rs_mode = os.environ.get("FT_ZERO3_RS", "ce")   # ce | p2p | nccl
+        use_p2p_rs = use_symm and rs_mode in ("ce", "p2p")
+        offsets, grad_offsets = [], []
         if use_symm:
             from femtotron_b200.parallel.symm import SymmetricAllocator, SymmetricHeap
             alloc = SymmetricAllocator()
             es = groups[0].compute.element_size()
+            al = ParamGroupCluster.SYMM_ALIGN
             for i, (u, pgs) in enumerate(unit_pgs):
-                offsets.append(alloc.reserve(f"unit{i}", ParamGroupCluster.shard_numel(pgs, self.dp_size) * es))
+                shard = ParamGroupCluster.shard_numel(pgs, self.dp_size, al)
+                offsets.append(alloc.reserve(f"unit{i}", shard * es))
+                if use_p2p_rs:
+                    # bf16 gradient buffer of the whole unit + one flag per rank
+                    grad_offsets.append((alloc.reserve(f"grad{i}", shard * self.dp_size * es),
+                                         alloc.reserve(f"flags{i}", 4 * self.dp_size)))
             self.heap = SymmetricHeap(self.dp_group, None, alloc.size, dev)
             self._barrier_t = torch.zeros(1, device=dev)
         for i, (u, pgs) in enumerate(unit_pgs):
             c = ParamGroupCluster(names.get(u, type(u).__name__) or "<root>", u, pgs, self.dp_group,
                                   master_dtype, comm_stream=self.comm_stream,
-                                  symm=(self.heap, offsets[i]) if use_symm else None)
+                                  symm=(self.heap, offsets[i]) if use_symm else None,
+                                  symm_grad=grad_offsets[i] if use_p2p_rs else None)
             self.clusters.append(c)
+        if use_p2p_rs:
+            self.rs_stream = torch.cuda.Stream(device=dev)
+            for c in self.clusters:
+                c.rs_mode = rs_mode
+                c.rs_stream = self.rs_stream
         for i, c in enumerate(self.clusters):
             c.index = i
             if not c.direct:
                 self._install_hooks(c)
-        # free (non-unit) parameters accumulate an fp32 gradient in place
+        # free (non-unit) parameters accumulate an fp32 gradient in place; with dp > 1 on CUDA
+        # their all-reduce starts on a side stream as soon as the last micro-batch's backward
+        # has produced the gradient (lm_head and the final norm come first in the backward)
         for pg in groups:
             if pg.cluster is None and pg.compute.requires_grad:
                 pg.compute.main_grad = torch.zeros(pg.compute.shape, dtype=torch.float32,
                                                    device=pg.compute.device)
+                if self.comm_stream is not None:
+                    pg.compute._ft_grad_ready = (lambda p=pg.compute: self._free_grad_ready(p))
+        if self.comm_stream is not None:
+            self.ar_stream = torch.cuda.Stream(device=dev)
+        self.shards_written()
         return self.clusters
+
+    def shards_written(self) -> None:
+        """Call after this rank wrote its parameter shards into symmetric memory (construction,
+        checkpoint load): peers' copy engines read those shards directly, so every rank's
+        writes must be complete before any rank gathers."""
+        if self.heap is not None:
+            torch.cuda.synchronize(self.heap.device)
+            dist.barrier(group=self.dp_group)
+
+    def _free_grad_ready(self, p) -> None:
+        if not self._sync_enabled:
+            return
+        mg = p.main_grad
+        cur = torch.cuda.current_stream(mg.device)
+        self.ar_stream.wait_stream(cur)
+        with torch.cuda.stream(self.ar_stream):
+            dist.all_reduce(mg, op=dist.ReduceOp.AVG, group=self.dp_group)
+        self._early_reduced.add(id(mg))
 
     # ------------------------------------------------------------------ hooks
     def _install_hooks(self, c: ParamGroupCluster) -> None:
@@ -144,8 +187,12 @@ class ZeRO3Strategy:
                 n.prefetch()
 
     def _post_forward(self, c):
-        if not c.in_backward:
-            c.reshard()
+        if c.in_backward:
+            return
+        # the last unit's backward comes right after the forward: keep it gathered
+        if c.index == len(self.clusters) - 1 and torch.is_grad_enabled():
+            return
+        c.reshard()
 
     def _pre_backward(self, c):
         self._throttle()
@@ -158,10 +205,14 @@ class ZeRO3Strategy:
                 n.prefetch()
 
     def _post_backward(self, c):
+        c.in_backward = False
         if self._sync_enabled:
             c.reduce_scatter_grads()
+        elif c.index == 0:
+            # under no_sync another micro-batch follows and starts with this unit; its
+            # parameters cannot change before then (no optimizer step), so keep them
+            return
         c.reshard()
-        c.in_backward = False
 
     # ------------------------------------------------------------------ strategy protocol
     def prepare_for_backward(self, groups: list) -> None:
@@ -169,21 +220,32 @@ class ZeRO3Strategy:
 
     def reduce_grads(self, compute_grads: list, targets: list, target_specs: list) -> list:
         """Free parameters: all-reduce (AVG) over DP and return fp32 gradients."""
+        from femtotron_b200.utils.comm_timing import TIMER
         if self.comm_stream is not None:
-            torch.cuda.current_stream(self.comm_stream.device).wait_stream(self.comm_stream)
+            cur = torch.cuda.current_stream(self.comm_stream.device)
+            with TIMER.wait("grad_reduce"):
+                cur.wait_stream(self.comm_stream)
+                cur.wait_stream(self.ar_stream)
+                if self.rs_stream is not None:
+                    cur.wait_stream(self.rs_stream)
+        early, self._early_reduced = self._early_reduced, set()
         out = []
         for g, t in zip(compute_grads, targets):
             if g is None:
                 out.append(torch.zeros_like(t))
                 continue
-            if self.dp_size > 1:
-                dist.all_reduce(g, op=dist.ReduceOp.AVG, group=self.dp_group)
+            if self.dp_size > 1 and id(g) not in early:
+                with TIMER.wait("free_grad_allreduce"):
+                    dist.all_reduce(g, op=dist.ReduceOp.AVG, group=self.dp_group)
             out.append(g if g.dtype == t.dtype else g.to(t.dtype))
         return out
 
     def wait_comm(self) -> None:
         if self.comm_stream is not None:
-            torch.cuda.current_stream(self.comm_stream.device).wait_stream(self.comm_stream)
+            cur = torch.cuda.current_stream(self.comm_stream.device)
+            for st in (self.comm_stream, self.ar_stream, self.rs_stream):
+                if st is not None:
+                    cur.wait_stream(st)
 
     def gather_weights(self, groups: list) -> None:
         for g in groups:
@@ -198,7 +260,14 @@ class ZeRO3Strategy:
         # updates it because every gather of a step precedes that step's last reduce-scatter
         # on the same communication stream, and the update waits for that reduce-scatter.)
         if self.heap is not None:
-            dist.all_reduce(self._barrier_t, group=self.dp_group)
+            from femtotron_b200.utils.comm_timing import TIMER
+            with TIMER.wait("step_barrier"):
+                dist.all_reduce(self._barrier_t, group=self.dp_group)
+        # a unit still gathered now (kept across a forward whose backward never ran) holds
+        # pre-update parameters
+        for c in self.clusters:
+            if not c.in_backward:
+                c.reshard()
 
     def grads_are_dp_sharded(self) -> bool:
         return True
@@ -223,6 +292,7 @@ class ZeRO3Strategy:
 
     def force_reshard_all(self) -> None:
         """Exception recovery: drop every gathered buffer and pending prefetch."""
+        self._early_reduced = set()
         for c in self.clusters:
             try:
                 c._prefetch = None

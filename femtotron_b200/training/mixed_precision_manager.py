@@ -225,6 +225,9 @@ class MixedPrecisionManager:
         for c in self.clusters:
             if c.name in cm:
                 c.load_state_dict(cm[c.name])
+        written = getattr(self.strategy, "shards_written", None)
+        if written is not None:
+            written()   # peers read the rewritten shards directly: order them before any gather
         self.inner.load_state_dict(sd["inner_optimizer"])
         gas = sd.get("grad_accumulators", {})
         for g, ga in zip(self.groups, self.grad_accs):

@@ -1,0 +1,46 @@
+"""Exposed-communication timer: how long the compute stream is blocked on communication.
+
+Every place where the compute stream waits for a communication stream or runs a collective
+inline is wrapped in ``TIMER.wait(kind)``: a CUDA event is recorded on the compute stream
+right before and right after the wait, and since nothing else is enqueued between the two,
+their distance is device time the compute stream spent blocked.  Enabled by
+FT_COMM_TIMING=1 (otherwise the context manager does nothing).  The reference has no such
+measurement (it prints host-timed tokens/s only, femtotron/training/trainer.py:241-250).
+"""
+from __future__ import annotations
+
+import os
+from collections import defaultdict
+from contextlib import contextmanager
+
+import torch
+
+
+class CommWaitTimer:
+    def __init__(self):
+        self.enabled = os.environ.get("FT_COMM_TIMING") == "1"
+        self._pending: list[tuple[str, torch.cuda.Event, torch.cuda.Event]] = []
+
+    @contextmanager
+    def wait(self, kind: str):
+        if not self.enabled or not torch.cuda.is_available():
+            yield
+            return
+        a = torch.cuda.Event(enable_timing=True)
+        a.record()
+        yield
+        b = torch.cuda.Event(enable_timing=True)
+        b.record()
+        self._pending.append((kind, a, b))
+
+    def collect(self) -> dict:
+        """Milliseconds blocked per kind since the last call (synchronises on the events)."""
+        out: dict[str, float] = defaultdict(float)
+        for kind, a, b in self._pending:
+            b.synchronize()
+            out[kind] += a.elapsed_time(b)
+        self._pending.clear()
+        return dict(out)
+
+
+TIMER = CommWaitTimer()

@@ -161,7 +161,29 @@ def op_xent(name):
     return {"kind": "bytes", "bytes": logits.numel() * 2, "run": run, "name": name}
 
 
+def op_p2p_copy(name, streams: int):
+    """Copy-engine peer copy cuda:1 -> cuda:0 of one ZeRO-3 unit half (218 MB), split over
+    `streams` streams (needs two visible GPUs)."""
+    n = 109 * 1000 * 1000
+    src = torch.randn(n, device="cuda:1").to(torch.bfloat16)
+    dst = torch.empty(n, device="cuda:0", dtype=torch.bfloat16)
+    ss = [torch.cuda.Stream(device="cuda:0") for _ in range(streams)]
+    parts = list(zip(dst.chunk(streams), src.chunk(streams)))
+
+    def run():
+        cur = torch.cuda.current_stream()
+        for st, (d, s_) in zip(ss, parts):
+            st.wait_stream(cur)
+            with torch.cuda.stream(st):
+                d.copy_(s_, non_blocking=True)
+        for st in ss:
+            cur.wait_stream(st)
+    return {"kind": "bytes", "bytes": n * 2, "run": run, "name": name}
+
+
 OPS = {
+    "p2p_copy_1": lambda: op_p2p_copy("p2p_copy_1", 1),
+    "p2p_copy_4": lambda: op_p2p_copy("p2p_copy_4", 4),
     "gemm_qkv": lambda: op_gemm("gemm_qkv", T, (NQ + 2 * NKV) * D, H),
     "gemm_o": lambda: op_gemm("gemm_o", T, H, NQ * D),
     "gemm_gateup": lambda: op_gemm("gemm_gateup", T, 2 * FF, H),
@@ -188,7 +210,7 @@ def main(argv=None):
     ap.add_argument("--compare", action="store_true", help="also time the torch library op")
     args = ap.parse_args(argv)
     pk = peaks()
-    names = sorted(OPS) if args.op == "all" else [args.op]
+    names = sorted(n for n in OPS if not n.startswith("p2p")) if args.op == "all" else [args.op]
     for n in names:
         spec = OPS[n]()
         flush = spec["kind"] == "flops"  # memory-bound ops already use inputs larger than L2

@@ -84,12 +84,21 @@ def main():
     ctx = ParallelContext(OrderedDict(dp=dist.get_world_size()))
     z0 = train(0, ctx, cfg, sd)
     z3 = train(3, ctx, cfg, sd)
+    os.environ["FT_ZERO3_RS"] = "nccl"      # NCCL reduce-scatter for comparison
+    z3_nccl = train(3, ctx, cfg, sd)
+    os.environ["FT_ZERO3_RS"] = "p2p"       # single-kernel P2P reduce-scatter
+    z3_p2p = train(3, ctx, cfg, sd)
+    os.environ.pop("FT_ZERO3_RS")
     t1, g1 = tp_loss(cfg, sd, 1, False)
     t2, g2 = tp_loss(cfg, sd, 2, True)
     worst = max(abs(g1[k] - g2[k]) / (g1[k] + 1e-12) for k in g1)
-    res = {"z0": z0, "z3": z3, "tp1": t1, "tp2_sp": t2, "grad_norm_rel_err": worst}
+    res = {"z0": z0, "z3": z3, "z3_nccl": z3_nccl, "z3_p2p": z3_p2p, "tp1": t1, "tp2_sp": t2, "grad_norm_rel_err": worst}
     if dist.get_rank() == 0:
         print("RESULT " + json.dumps(res), flush=True)
+        out = os.environ.get("FT_TEST_RESULT_DIR")
+        if out:
+            with open(os.path.join(out, "zero_tp_check.json"), "w") as f:
+                json.dump(res, f)
     dist.barrier()
     dist.destroy_process_group()
 
