@@ -17,6 +17,10 @@ Two measurements of our implementation, each over K steps after W warm-up steps:
 The per-step working set (weights, optimizer state, activations: >100 GB) exceeds the 126 MB
 L2 cache, so no explicit L2 flush is needed between steps.
 
+``--config llama2-13b-tp-sp`` measures the secondary BASELINE configuration instead: Llama-2-13B
+with tensor parallelism over all N GPUs plus sequence parallelism (DP=1, micro-batch 2,
+seq 4096, no activation checkpointing; strong scaling).
+
 ``--impl reference`` runs the unmodified reference (installed under baseline/_ref) through
 its own public API on the same configuration and prints the same JSON line with
 "impl": "reference".
@@ -42,24 +46,46 @@ LLAMA3_8B = dict(hidden_size=4096, intermediate_size=14336, num_attention_heads=
                  tie_word_embeddings=False)
 
 
+LLAMA2_13B = dict(hidden_size=5120, intermediate_size=13824, num_attention_heads=40,
+                  num_key_value_heads=40, num_hidden_layers=40, vocab_size=32000,
+                  max_position_embeddings=4096, rms_norm_eps=1e-5, rope_theta=10000.0,
+                  tie_word_embeddings=False)
+
+# --config: the default is the headline benchmark; the others are secondary BASELINE configs
+CONFIGS = {
+    "llama3-8b-zero3": dict(model=LLAMA3_8B, name="Llama-3-8B", micro_batch=1, grad_accum=8, seq=4096),
+    "llama2-13b-tp-sp": dict(model=LLAMA2_13B, name="Llama-2-13B", micro_batch=2, grad_accum=1, seq=4096),
+}
+
+
 def parse():
     ap = argparse.ArgumentParser()
+    ap.add_argument("--config", default="llama3-8b-zero3", choices=sorted(CONFIGS),
+                    help="llama3-8b-zero3: ZeRO-3 over all GPUs (headline); llama2-13b-tp-sp: "
+                         "tensor parallel over all GPUs with sequence parallelism, DP=1")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--seq", type=int, default=4096)
-    ap.add_argument("--micro-batch", type=int, default=1)
-    ap.add_argument("--grad-accum", type=int, default=8)
+    ap.add_argument("--seq", type=int, default=None)
+    ap.add_argument("--micro-batch", type=int, default=None)
+    ap.add_argument("--grad-accum", type=int, default=None)
     ap.add_argument("--layers", type=int, default=None,
                     help="override layer count (debug only; results are then not the benchmark)")
     ap.add_argument("--no-e2e", action="store_true")
-    return ap.parse_args()
+    args = ap.parse_args()
+    c = CONFIGS[args.config]
+    args.seq = args.seq or c["seq"]
+    args.micro_batch = args.micro_batch or c["micro_batch"]
+    args.grad_accum = args.grad_accum or c["grad_accum"]
+    args.tp = args.config == "llama2-13b-tp-sp"
+    args.model_name = c["name"]
+    return args
 
 
-def model_config(layers=None):
+def model_config(layers=None, config="llama3-8b-zero3"):
     from transformers import LlamaConfig
-    kw = dict(LLAMA3_8B)
+    kw = dict(CONFIGS[config]["model"])
     if layers:
         kw["num_hidden_layers"] = layers
     cfg = LlamaConfig(**kw)
@@ -107,18 +133,20 @@ def build_ours(cfg, args, ctx, device):
     from femtotron_b200.training.ckpt_policy import by_class
     from femtotron_b200.models.layers import LlamaDecoderLayer
     torch.manual_seed(1234)
-    model = build_llama_model(cfg, ctx)
+    model = build_llama_model(cfg, ctx, sequence_parallel=args.tp and ctx.tp_size > 1)
     materialize_model(model, device, dtype=torch.bfloat16, init_std=0.02)
     total_steps = args.warmup + 2 * args.steps + 10
     tc = TrainConfig(train_steps=total_steps, grad_accum_steps=args.grad_accum, grad_clip=None,
                      master_dtype=torch.float32, param_dtype=torch.bfloat16, log_interval=10 ** 9,
                      checkpoint_interval=10 ** 9, warmup_steps=2, lr=3e-4)
-    strategy = create_sharding_strategy(ctx, ZeROConfig(stage=3, wrap_policy=llama_wrap_policy))
+    zc = ZeROConfig(stage=0) if args.tp else ZeROConfig(stage=3, wrap_policy=llama_wrap_policy)
+    strategy = create_sharding_strategy(ctx, zc)
     mp = MixedPrecisionManager(model, ctx, get_llama_parallel_plan(), tc, FusedAdamW,
                                dict(lr=3e-4, betas=(0.9, 0.95), eps=1e-8),
                                get_param_groups(model, 0.01), sharding_strategy=strategy)
-    apply_activation_checkpointing(model, by_class(LlamaDecoderLayer), use_reentrant=False,
-                                   preserve_rng_state=False)
+    if not args.tp:   # the ZeRO-3 config trains with full activation checkpointing
+        apply_activation_checkpointing(model, by_class(LlamaDecoderLayer), use_reentrant=False,
+                                       preserve_rng_state=False)
     sched = create_lr_schedule(mp.inner, tc.warmup_steps, total_steps, 0.1)
     gsync = create_grad_synchronizer(mp.groups, ctx, strategy)
     return model, mp, sched, gsync, tc
@@ -135,14 +163,14 @@ def run_ours(args):
 
     rank, world, local = init_distributed("nccl", timeout_s=int(os.environ.get("FT_PG_TIMEOUT", "600")))
     device = torch.device("cuda", local)
-    cfg = model_config(args.layers)
-    ctx = ParallelContext(OrderedDict(dp=world))
+    cfg = model_config(args.layers, args.config)
+    ctx = ParallelContext(OrderedDict(tp=world) if args.tp else OrderedDict(dp=world))
     model, mp, sched, gsync, tc = build_ours(cfg, args, ctx, device)
     ga, mb, S = args.grad_accum, args.micro_batch, args.seq
 
     # ---- device-timed phase: micro-batches pre-staged on the device
     g = torch.Generator(device="cpu")
-    g.manual_seed(1000 + rank)
+    g.manual_seed(1000 + ctx.dp_rank)   # tensor-parallel peers share their batch
     dev_batches = [torch.randint(0, cfg.vocab_size, (mb, S), generator=g).to(device) for _ in range(ga)]
 
     class DevIter:
@@ -184,9 +212,11 @@ def run_ours(args):
         comm_tot: dict = {}
         for i in range(args.steps):
             info = trainer._train_one_step_standard(it)
+            TIMER.mark("optimizer")
             trainer.grad_sync.sync_gradients()
             mp.step()
             sched.step()
+            TIMER.mark(None)
             losses.append(info)
             if TIMER.enabled:  # diagnostic mode: syncs on the step's wait events
                 for k, v in TIMER.collect().items():
@@ -203,13 +233,14 @@ def run_ours(args):
     loss_last = float(losses[-1].item())
     ext.check_kernel_errors(device)
     ms_per_step = dev_ms / args.steps
-    tokens_per_step = ga * mb * S * world
+    dp = ctx.dp_size
+    tokens_per_step = ga * mb * S * dp
     value = tokens_per_step / (ms_per_step / 1e3)
 
     # ---- end-to-end phase through the public API (pinned host -> device, loss -> host)
     e2e = None
     if not args.no_e2e:
-        ds = SyntheticTokens(num_samples=ga * mb * world * (args.steps + 2), seq_len=S,
+        ds = SyntheticTokens(num_samples=ga * mb * dp * (args.steps + 2), seq_len=S,
                              vocab_size=cfg.vocab_size, seed=7)
         dl = DistributedDataLoader(ds, ctx, mb, simple_pretrain_collator, num_workers=2, pin_memory=True)
         trainer.dataloader = dl
@@ -239,12 +270,14 @@ def run_ours(args):
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 2),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic (uniform random token ids, random-init weights)",
-        "config": {"model": "Llama-3-8B" if not args.layers else f"Llama-3-8B-{args.layers}L(debug)",
-                   "global_batch": ga * mb * world, "micro_batch": mb, "grad_accum": ga,
-                   "seq_len": S, "parallelism": f"zero3-dp{world}", "activation_checkpointing": "full",
-                   "optimizer": "AdamW fp32 master", "l2": "per-step working set >100 GB >> 126 MB L2 (no flush needed)"},
+        "higher_is_better": True, "scaling": "strong" if args.tp else "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic (uniform random token ids, random-init weights)",
+        "config": {"model": args.model_name if not args.layers else f"{args.model_name}-{args.layers}L(debug)",
+                   "global_batch": ga * mb * dp, "micro_batch": mb, "grad_accum": ga,
+                   "seq_len": S,
+                   "parallelism": f"tp{world}-sp" if args.tp else f"zero3-dp{world}",
+                   "activation_checkpointing": "none" if args.tp else "full",
+                   "optimizer": "AdamW fp32 master", "l2": "per-step working set (weights, optimizer state, activations) >> 126 MB L2 (no flush needed)"},
         "mfu": round(mfu, 4), "mfu_peak_tflops": pk["bf16_tflops"],
         "flops_per_token": flops_per_token(cfg, S),
         "loss_last": loss_last,
@@ -263,6 +296,9 @@ def run_ours(args):
 
 # ----------------------------------------------------------------------------- reference arm
 def run_reference(args):
+    if args.config != "llama3-8b-zero3":
+        emit({"impl": "reference", "unavailable": "the reference arm covers the headline configuration only"})
+        return
     ref_root = os.path.join(HERE, "baseline", "_ref")
     if not os.path.isdir(os.path.join(ref_root, "femtotron")):
         emit({"impl": "reference", "unavailable": "reference not installed under baseline/_ref"})

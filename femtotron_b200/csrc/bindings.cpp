@@ -39,12 +39,12 @@ torch::Tensor tensor_at(int64_t ptr, int64_t numel, torch::ScalarType dtype, int
 void copy_from_ptrs(const std::vector<int64_t>& dsts, const std::vector<int64_t>& srcs,
                     const std::vector<int64_t>& nbytes);
 void reduce_slices_f32(const std::vector<int64_t>& src_ptrs, torch::Tensor& acc, int64_t n,
-                       double scale, bool accumulate);
+                       double scale, bool accumulate, bool src_f32);
 void p2p_publish(const std::vector<int64_t>& flag_ptrs, int64_t rank, int64_t epoch);
 void p2p_reduce_scatter(const std::vector<int64_t>& buf_ptrs, int64_t flags_local,
                         const std::vector<int64_t>& flag_ptrs, torch::Tensor& acc, int64_t shard,
                         int64_t rank, int64_t epoch, double scale, bool accumulate,
-                        torch::Tensor& err);
+                        torch::Tensor& err, bool src_f32);
 void gemm_tc_fused(const torch::Tensor& A, const torch::Tensor& B, torch::Tensor& D, bool a_mn,
                    bool b_mn, int64_t mode,
                    const c10::optional<torch::Tensor>& R, const c10::optional<torch::Tensor>& GU,

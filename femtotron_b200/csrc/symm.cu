@@ -90,11 +90,12 @@ void copy_from_ptrs(const std::vector<int64_t>& dsts, const std::vector<int64_t>
 //       flags_of_rank_r[this rank] = epoch for every r (release, system scope);
 //   p2p_reduce_scatter (communication stream): wait (bounded) until every peer's flag in the
 //       local array is >= epoch, then read slice [rank*shard, (rank+1)*shard) of every peer's
-//       buffer over NVLink and write  acc[i] (+)= scale * sum_r buf_r[rank*shard + i]  in fp32.
+//       buffer over NVLink and write  acc[i] (+)= scale * sum_r buf_r[rank*shard + i]  in fp32
+//       (the buffers hold bf16 or fp32 gradients).
 // Peers may reuse their buffers only after every rank's reduction has finished; the caller
 // provides that ordering (a device-side barrier between steps).
 struct RSArgs {
-  const __nv_bfloat16* bufs[8];  // every rank's full gradient buffer (peer addresses)
+  const void* bufs[8];           // every rank's full gradient buffer (peer addresses), bf16 or fp32
   volatile int* flags_local;     // this rank's flag array [world]
   int* flags_remote[8];          // flag arrays of every rank (peer addresses)
   float* acc;                    // local fp32 shard accumulator
@@ -138,6 +139,25 @@ __device__ __forceinline__ bool wait_peers(const RSArgs& a) {
   return true;
 }
 
+// Load 8 consecutive elements (bf16 or fp32) as fp32.
+__device__ __forceinline__ void load8(const void* p, int64_t i, float (&f)[8], bool f32) {
+  if (f32) {
+    const float4* q = reinterpret_cast<const float4*>(static_cast<const float*>(p) + i);
+    const float4 a = q[0], b = q[1];
+    f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+  } else {
+    const uint4 q = *reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(p) + i);
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&q);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 t = __bfloat1622float2(h[j]);
+      f[2 * j] = t.x;
+      f[2 * j + 1] = t.y;
+    }
+  }
+}
+
+template <bool F32>
 __global__ void p2p_reduce_scatter_kernel(RSArgs a) {
   if (a.wait) {
     __shared__ int ok;
@@ -150,20 +170,13 @@ __global__ void p2p_reduce_scatter_kernel(RSArgs a) {
   for (int64_t v = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; v < nvec;
        v += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     float s[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    uint4 q[8];
-#pragma unroll
-    for (int r = 0; r < 8; ++r)
-      if (r < a.world) q[r] = *reinterpret_cast<const uint4*>(a.bufs[r] + base + v * 8);
 #pragma unroll
     for (int r = 0; r < 8; ++r) {
       if (r >= a.world) break;
-      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&q[r]);
+      float f[8];
+      load8(a.bufs[r], base + v * 8, f, F32);
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float2 f = __bfloat1622float2(h[j]);
-        s[2 * j] += f.x;
-        s[2 * j + 1] += f.y;
-      }
+      for (int j = 0; j < 8; ++j) s[j] += f[j];
     }
     float4* d = reinterpret_cast<float4*>(a.acc + v * 8);
     float4 o0 = make_float4(s[0] * a.scale, s[1] * a.scale, s[2] * a.scale, s[3] * a.scale);
@@ -178,6 +191,15 @@ __global__ void p2p_reduce_scatter_kernel(RSArgs a) {
   }
 }
 
+void launch_reduce(const RSArgs& a, bool f32, int grid) {
+  auto st = at::cuda::getCurrentCUDAStream();
+  if (f32)
+    p2p_reduce_scatter_kernel<true><<<grid, 256, 0, st>>>(a);
+  else
+    p2p_reduce_scatter_kernel<false><<<grid, 256, 0, st>>>(a);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 namespace {
 RSArgs make_rs_args(const std::vector<int64_t>& buf_ptrs, const std::vector<int64_t>& flag_ptrs,
                     int64_t rank, int64_t epoch) {
@@ -186,7 +208,7 @@ RSArgs make_rs_args(const std::vector<int64_t>& buf_ptrs, const std::vector<int6
   TORCH_CHECK(buf_ptrs.empty() || static_cast<int>(buf_ptrs.size()) == world);
   RSArgs a{};
   for (int r = 0; r < world; ++r) {
-    if (!buf_ptrs.empty()) a.bufs[r] = reinterpret_cast<const __nv_bfloat16*>(buf_ptrs[r]);
+    if (!buf_ptrs.empty()) a.bufs[r] = reinterpret_cast<const void*>(buf_ptrs[r]);
     a.flags_remote[r] = reinterpret_cast<int*>(flag_ptrs[r]);
   }
   a.world = world;
@@ -206,7 +228,7 @@ void p2p_publish(const std::vector<int64_t>& flag_ptrs, int64_t rank, int64_t ep
 void p2p_reduce_scatter(const std::vector<int64_t>& buf_ptrs, int64_t flags_local,
                         const std::vector<int64_t>& flag_ptrs, torch::Tensor& acc, int64_t shard,
                         int64_t rank, int64_t epoch, double scale, bool accumulate,
-                        torch::Tensor& err) {
+                        torch::Tensor& err, bool src_f32) {
   TORCH_CHECK(acc.scalar_type() == at::kFloat && acc.is_contiguous() && acc.numel() >= shard);
   TORCH_CHECK(shard % 8 == 0, "p2p_reduce_scatter: shard must be a multiple of 8 elements");
   RSArgs a = make_rs_args(buf_ptrs, flag_ptrs, rank, epoch);
@@ -226,21 +248,20 @@ void p2p_reduce_scatter(const std::vector<int64_t>& buf_ptrs, int64_t flags_loca
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int64_t nvec = shard / 8;
   const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((nvec + 255) / 256, sms)));
-  p2p_reduce_scatter_kernel<<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(a);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  launch_reduce(a, src_f32, grid);
 }
 
 // Local reduction of `world` bf16 slices (already in this GPU's memory, e.g. pulled from the
 // peers by copy engines) into the fp32 shard: acc (+)= scale * sum_r src_r.  No waits.
 void reduce_slices_f32(const std::vector<int64_t>& src_ptrs, torch::Tensor& acc, int64_t n,
-                       double scale, bool accumulate) {
+                       double scale, bool accumulate, bool src_f32) {
   TORCH_CHECK(acc.scalar_type() == at::kFloat && acc.is_contiguous() && acc.numel() >= n);
   TORCH_CHECK(n % 8 == 0, "reduce_slices_f32: n must be a multiple of 8");
   const int world = static_cast<int>(src_ptrs.size());
   TORCH_CHECK(world >= 1 && world <= 8);
   RSArgs a{};
   for (int r = 0; r < world; ++r) {
-    a.bufs[r] = reinterpret_cast<const __nv_bfloat16*>(src_ptrs[r]);
+    a.bufs[r] = reinterpret_cast<const void*>(src_ptrs[r]);
     TORCH_CHECK((src_ptrs[r] & 15) == 0, "reduce_slices_f32: 16-byte aligned sources");
   }
   a.world = world;
@@ -255,8 +276,7 @@ void reduce_slices_f32(const std::vector<int64_t>& src_ptrs, torch::Tensor& acc,
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int64_t nvec = n / 8;
   const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((nvec + 255) / 256, 2 * sms)));
-  p2p_reduce_scatter_kernel<<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(a);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  launch_reduce(a, src_f32, grid);
 }
 
 }  // namespace ft

@@ -35,6 +35,12 @@ from torch import nn
 
 from .cluster_sharding_spec import compute_cluster_layout
 
+import os
+
+# FT_ZERO3_DEBUG_NOCOPY=1 skips the parameter transfer of every gather (wrong numerics; used
+# only to separate the cost of the transfer from the cost of its bookkeeping)
+_DEBUG_NOCOPY = os.environ.get("FT_ZERO3_DEBUG_NOCOPY") == "1"
+
 
 class ParamGroupCluster:
     def __init__(self, name: str, module: nn.Module, param_groups: list, dp_group,
@@ -77,6 +83,10 @@ class ParamGroupCluster:
         # "p2p" (one kernel that waits for the flags and loads the peers' slices itself)
         self.rs_mode = "ce"
         self.rs_stream = None
+        # dtype of the unsharded gradient buffer the backward accumulates into (dp > 1);
+        # fp32 lets the weight-gradient GEMMs accumulate through the TMA reduce-add epilogue
+        # and keeps micro-batch accumulation exact; the strategy may choose bf16 to save memory
+        self.grad_dtype = self.compute_dtype
 
         self.flat_param_shard = self._initialize_flat_param_shard()
         self.master = self.flat_param_shard.to(master_dtype)
@@ -120,6 +130,8 @@ class ParamGroupCluster:
 
     def _gather_into(self, buf: torch.Tensor) -> None:
         """All-gather the packed parameters into `buf` on the current stream."""
+        if _DEBUG_NOCOPY:   # timing diagnostic only: bookkeeping without the transfer
+            return
         if self.symm is None:
             dist.all_gather_into_tensor(buf, self.flat_param_shard, group=self.dp_group)
             return
@@ -196,10 +208,10 @@ class ParamGroupCluster:
             # persistent symmetric buffer: every peer finished reading it in the previous
             # step (the optimizer step is followed by a device-side barrier)
             heap = self.symm[0]
-            gb = heap.view(self.symm_grad[0], self.padded_size, self.compute_dtype)
+            gb = heap.view(self.symm_grad[0], self.padded_size, self.grad_dtype)
             gb.zero_()
         else:
-            gb = torch.zeros(self.padded_size, dtype=self.compute_dtype, device=self.device)
+            gb = torch.zeros(self.padded_size, dtype=self.grad_dtype, device=self.device)
         self._grad_buffer = gb
         for pg, l in zip(self.param_groups, self.layouts):
             pg.compute.main_grad = gb[l.global_offset:l.global_end].view(l.original_shape)
@@ -249,23 +261,24 @@ class ParamGroupCluster:
         C.p2p_publish(flags, rank, ep)          # after this unit's backward kernels
         st = self.rs_stream or self.comm_stream
         st.wait_stream(cur)
+        f32 = self.grad_dtype == torch.float32
         with torch.cuda.stream(st):
             if self.rs_mode == "p2p":
                 C.p2p_reduce_scatter([heap.peer_ptr(r, goff) for r in range(R)], flags[rank], flags,
                                      self.flat_grad_shard, self.shard_size, rank, ep, 1.0 / R,
-                                     accumulate, error_flag(self.device))
+                                     accumulate, error_flag(self.device), f32)
                 return
-            nb = self.shard_size * 2
+            nb = self.shard_size * (4 if f32 else 2)
             for r in range(R):                  # peers' flags, waited in the stream (no SMs)
                 if r != rank:
                     C.stream_wait_geq(flags[rank] + 4 * r, ep)
-            stage = torch.empty(R - 1, self.shard_size, dtype=self.compute_dtype, device=self.device)
+            stage = torch.empty(R - 1, self.shard_size, dtype=self.grad_dtype, device=self.device)
             peers = [r for r in range(R) if r != rank]
             C.copy_from_ptrs([stage[i].data_ptr() for i in range(R - 1)],
                              [heap.peer_ptr(r, goff) + rank * nb for r in peers], [nb] * (R - 1))
             own = heap.peer_ptr(rank, goff) + rank * nb
             C.reduce_slices_f32([own] + [stage[i].data_ptr() for i in range(R - 1)],
-                                self.flat_grad_shard, self.shard_size, 1.0 / R, accumulate)
+                                self.flat_grad_shard, self.shard_size, 1.0 / R, accumulate, f32)
 
     def populate_master_grad(self) -> None:
         """Point the optimizer's views at the reduced fp32 gradient (no copy)."""

@@ -52,6 +52,10 @@ class ZeRO3Strategy:
         self._inflight: list = []
         self.ar_stream = None
         self.rs_stream = None
+        # keep every unit gathered from its first use in a step until the step ends (trades
+        # one full bf16 copy of the unit parameters for 2*grad_accum-1 fewer gathers per
+        # unit and step); off by default: ZeRO-3 reshards after every use
+        self.keep_in_step = os.environ.get("FT_ZERO3_KEEP_IN_STEP") == "1"
         self._early_reduced: set[int] = set()
 
     def make_master(self, compute: nn.Parameter, master_dtype: torch.dtype):
@@ -93,6 +97,7 @@ class ZeRO3Strategy:
         use_symm = self.symmetric and dev.type == "cuda" and self.dp_size > 1
         rs_mode = os.environ.get("FT_ZERO3_RS", "ce")   # ce | p2p | nccl
         use_p2p_rs = use_symm and rs_mode in ("ce", "p2p")
+        grad_dtype = self._pick_grad_dtype(unit_pgs, dev)
         offsets, grad_offsets = [], []
         if use_symm:
             from femtotron_b200.parallel.symm import SymmetricAllocator, SymmetricHeap
@@ -104,7 +109,8 @@ class ZeRO3Strategy:
                 offsets.append(alloc.reserve(f"unit{i}", shard * es))
                 if use_p2p_rs:
                     # bf16 gradient buffer of the whole unit + one flag per rank
-                    grad_offsets.append((alloc.reserve(f"grad{i}", shard * self.dp_size * es),
+                    ges = torch.tensor([], dtype=grad_dtype).element_size()
+                    grad_offsets.append((alloc.reserve(f"grad{i}", shard * self.dp_size * ges),
                                          alloc.reserve(f"flags{i}", 4 * self.dp_size)))
             self.heap = SymmetricHeap(self.dp_group, None, alloc.size, dev)
             self._barrier_t = torch.zeros(1, device=dev)
@@ -114,6 +120,8 @@ class ZeRO3Strategy:
                                   symm=(self.heap, offsets[i]) if use_symm else None,
                                   symm_grad=grad_offsets[i] if use_p2p_rs else None)
             self.clusters.append(c)
+        for c in self.clusters:
+            c.grad_dtype = grad_dtype
         if use_p2p_rs:
             self.rs_stream = torch.cuda.Stream(device=dev)
             for c in self.clusters:
@@ -144,6 +152,20 @@ class ZeRO3Strategy:
         if self.heap is not None:
             torch.cuda.synchronize(self.heap.device)
             dist.barrier(group=self.dp_group)
+
+    def _pick_grad_dtype(self, unit_pgs, dev) -> torch.dtype:
+        """fp32 unsharded gradient buffers when they fit comfortably (they are persistent when
+        they live in symmetric memory), else the compute dtype.  FT_ZERO3_GRAD_DTYPE=fp32|bf16
+        forces the choice."""
+        first = unit_pgs[0][1][0].compute.dtype
+        env = os.environ.get("FT_ZERO3_GRAD_DTYPE", "auto")
+        if env == "fp32":
+            return torch.float32
+        if env == "bf16" or dev.type != "cuda" or self.dp_size == 1:
+            return first
+        total = sum(pg.compute.numel() for _, pgs in unit_pgs for pg in pgs)
+        cap = torch.cuda.get_device_properties(dev).total_memory
+        return torch.float32 if total * 4 <= 0.25 * cap else first
 
     def _free_grad_ready(self, p) -> None:
         if not self._sync_enabled:
@@ -187,7 +209,7 @@ class ZeRO3Strategy:
                 n.prefetch()
 
     def _post_forward(self, c):
-        if c.in_backward:
+        if c.in_backward or (self.keep_in_step and torch.is_grad_enabled()):
             return
         # the last unit's backward comes right after the forward: keep it gathered
         if c.index == len(self.clusters) - 1 and torch.is_grad_enabled():
@@ -208,7 +230,7 @@ class ZeRO3Strategy:
         c.in_backward = False
         if self._sync_enabled:
             c.reduce_scatter_grads()
-        elif c.index == 0:
+        elif c.index == 0 or self.keep_in_step:
             # under no_sync another micro-batch follows and starts with this unit; its
             # parameters cannot change before then (no optimizer step), so keep them
             return

@@ -118,15 +118,20 @@ class Trainer:
         return {k: v.to(self.device, non_blocking=True) for k, v in batch.items()}
 
     def _train_one_step_standard(self, data_iter) -> torch.Tensor:
+        from femtotron_b200.utils.comm_timing import TIMER
         n = self.train_config.grad_accum_steps
         total = torch.zeros((), device=self.device)
         for micro in range(n):
             batch = self._batch_to_device(next(data_iter))
-            ctx = nullcontext() if micro == n - 1 else self.grad_sync.no_sync()
+            last = micro == n - 1
+            ctx = nullcontext() if last else self.grad_sync.no_sync()
             with ctx:
+                TIMER.mark("fwd_last" if last else "fwd")
                 out = self.model(input_ids=batch["input_ids"], labels=batch["labels"])
                 loss = out["loss"] / n
+                TIMER.mark("bwd_last" if last else "bwd")
                 loss.backward()
+                TIMER.mark(None)
                 total += loss.detach().float() * n
             self.mp_manager.accumulate_grads() if self.train_config.grad_acc_dtype is not None else None
         return total / n

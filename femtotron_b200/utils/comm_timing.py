@@ -20,6 +20,7 @@ class CommWaitTimer:
     def __init__(self):
         self.enabled = os.environ.get("FT_COMM_TIMING") == "1"
         self._pending: list[tuple[str, torch.cuda.Event, torch.cuda.Event]] = []
+        self._marks: list[tuple[str | None, torch.cuda.Event]] = []
 
     @contextmanager
     def wait(self, kind: str):
@@ -33,13 +34,28 @@ class CommWaitTimer:
         b.record()
         self._pending.append((kind, a, b))
 
+    def mark(self, label: str | None) -> None:
+        """Phase mark on the current stream: the device time until the next mark is added to
+        ``phase:<label>`` (label None only closes the previous phase)."""
+        if not self.enabled or not torch.cuda.is_available():
+            return
+        e = torch.cuda.Event(enable_timing=True)
+        e.record()
+        self._marks.append((label, e))
+
     def collect(self) -> dict:
-        """Milliseconds blocked per kind since the last call (synchronises on the events)."""
+        """Milliseconds blocked per kind, and per phase, since the last call (synchronises on
+        the events)."""
         out: dict[str, float] = defaultdict(float)
         for kind, a, b in self._pending:
             b.synchronize()
             out[kind] += a.elapsed_time(b)
         self._pending.clear()
+        for (label, a), (_, b) in zip(self._marks, self._marks[1:]):
+            if label is not None:
+                b.synchronize()
+                out["phase:" + label] += a.elapsed_time(b)
+        self._marks = self._marks[-1:] if self._marks and self._marks[-1][0] is not None else []
         return dict(out)
 
 
