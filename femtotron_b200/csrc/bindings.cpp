@@ -58,6 +58,9 @@ void sum_partials(const torch::Tensor& parts, const c10::optional<torch::Tensor>
                   torch::Tensor& out);
 void flash_fwd(const torch::Tensor& qkv, torch::Tensor& o, torch::Tensor& lse, int64_t B, int64_t S,
                int64_t nq, int64_t nkv, int64_t D, torch::Tensor& err);
+void flash_fwd_variant(const torch::Tensor& qkv, torch::Tensor& o, torch::Tensor& lse, int64_t B,
+                       int64_t S, int64_t nq, int64_t nkv, int64_t D, torch::Tensor& err,
+                       int64_t variant);
 void flash_bwd(const torch::Tensor& qkv, const torch::Tensor& o, const torch::Tensor& dout,
                const torch::Tensor& lse, torch::Tensor& dqkv, int64_t B, int64_t S, int64_t nq,
                int64_t nkv, int64_t D, torch::Tensor& err);
@@ -92,5 +95,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("stream_write", &ft::stream_write);
   m.def("sum_partials", &ft::sum_partials);
   m.def("flash_fwd", &ft::flash_fwd);
+  m.def("flash_fwd_variant", &ft::flash_fwd_variant);
   m.def("flash_bwd", &ft::flash_bwd);
 }

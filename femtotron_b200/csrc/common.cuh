@@ -354,6 +354,14 @@ FT_DEVICE float2 unpack_bf16x2(uint32_t v) {
   return __bfloat1622float2(b);
 }
 
+// 2^x by one special-function-unit instruction (ex2.approx.ftz; 2^-inf = 0, subnormal results
+// flush to zero, which the softmax probabilities that use it never need).
+FT_DEVICE float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // Warp / block reductions
 FT_DEVICE float warp_sum(float v) {
 #pragma unroll

@@ -280,10 +280,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll
         for (int c4 = 0; c4 < BQ / 8; ++c4) {
           const float4 l4 = L[c4];
-          pv[4 * c4 + 0] = exp2f(fmaf(__uint_as_float(sv[4 * c4 + 0]), p.scale_log2, -l4.x));
-          pv[4 * c4 + 1] = exp2f(fmaf(__uint_as_float(sv[4 * c4 + 1]), p.scale_log2, -l4.y));
-          pv[4 * c4 + 2] = exp2f(fmaf(__uint_as_float(sv[4 * c4 + 2]), p.scale_log2, -l4.z));
-          pv[4 * c4 + 3] = exp2f(fmaf(__uint_as_float(sv[4 * c4 + 3]), p.scale_log2, -l4.w));
+          pv[4 * c4 + 0] = ex2_approx(fmaf(__uint_as_float(sv[4 * c4 + 0]), p.scale_log2, -l4.x));
+          pv[4 * c4 + 1] = ex2_approx(fmaf(__uint_as_float(sv[4 * c4 + 1]), p.scale_log2, -l4.y));
+          pv[4 * c4 + 2] = ex2_approx(fmaf(__uint_as_float(sv[4 * c4 + 2]), p.scale_log2, -l4.z));
+          pv[4 * c4 + 3] = ex2_approx(fmaf(__uint_as_float(sv[4 * c4 + 3]), p.scale_log2, -l4.w));
         }
         if (diag) {  // query col0 + c sees key r only when col0 + c >= r
 #pragma unroll

@@ -158,7 +158,7 @@ struct AdamSeg {
   int64_t n;
   float wd;
   int g_f32;
-  int pad;
+  int pad;              // 1 when every array is 16-byte aligned (vector path)
 };
 
 struct AdamHyper {
@@ -166,10 +166,23 @@ struct AdamHyper {
   float bc1, bc2_sqrt;   // 1 - beta1^t, sqrt(1 - beta2^t)
 };
 
+__device__ __forceinline__ void adam_elem(float& p, float& m, float& v, float g, float decay,
+                                          float step_size, const AdamHyper& h) {
+  p *= decay;
+  m = h.beta1 * m + (1.f - h.beta1) * g;
+  v = h.beta2 * v + (1.f - h.beta2) * g * g;
+  p -= step_size * m / (sqrtf(v) / h.bc2_sqrt + h.eps);
+}
+
 // Blocks walk a chunk table: chunk c covers elements [start, start+len) of segment seg.
-__global__ void adamw_kernel(const AdamSeg* __restrict__ segs, const int2* __restrict__ chunks,
-                             const int64_t* __restrict__ chunk_start, AdamHyper h,
-                             const float* __restrict__ grad_scale, int chunk_len) {
+// Segments whose arrays are all 16-byte aligned (flag `pad`) move 4 elements per thread per
+// iteration with 16-byte loads/stores (8-byte for bf16), which keeps enough bytes in flight
+// to run near the HBM copy rate; the rest, and the ragged tail, go element by element.
+__global__ void __launch_bounds__(256) adamw_kernel(const AdamSeg* __restrict__ segs,
+                                                    const int2* __restrict__ chunks,
+                                                    const int64_t* __restrict__ chunk_start,
+                                                    AdamHyper h, const float* __restrict__ grad_scale,
+                                                    int chunk_len) {
   const int2 ch = chunks[blockIdx.x];
   const AdamSeg s = segs[ch.x];
   const int64_t start = chunk_start[blockIdx.x];
@@ -177,18 +190,43 @@ __global__ void adamw_kernel(const AdamSeg* __restrict__ segs, const int2* __res
   const float gs = grad_scale ? grad_scale[0] : 1.f;
   const float step_size = h.lr / h.bc1;
   const float decay = 1.f - h.lr * s.wd;
-  for (int64_t i = start + threadIdx.x; i < end; i += blockDim.x) {
+  float* __restrict__ P = s.p;
+  float* __restrict__ M = s.m;
+  float* __restrict__ Vv = s.v;
+  int64_t vec_end = start;
+  if (s.pad) {
+    vec_end = start + ((end - start) & ~int64_t(3));
+    for (int64_t i = start + 4 * threadIdx.x; i < vec_end; i += 4 * blockDim.x) {
+      float4 g4;
+      if (s.g_f32) {
+        g4 = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(s.g) + i);
+      } else {
+        const uint2 q = *reinterpret_cast<const uint2*>(reinterpret_cast<const __nv_bfloat16*>(s.g) + i);
+        const float2 a = unpack_bf16x2(q.x), b = unpack_bf16x2(q.y);
+        g4 = make_float4(a.x, a.y, b.x, b.y);
+      }
+      float4 p4 = *reinterpret_cast<const float4*>(P + i);
+      float4 m4 = *reinterpret_cast<const float4*>(M + i);
+      float4 v4 = *reinterpret_cast<const float4*>(Vv + i);
+      adam_elem(p4.x, m4.x, v4.x, g4.x * gs, decay, step_size, h);
+      adam_elem(p4.y, m4.y, v4.y, g4.y * gs, decay, step_size, h);
+      adam_elem(p4.z, m4.z, v4.z, g4.z * gs, decay, step_size, h);
+      adam_elem(p4.w, m4.w, v4.w, g4.w * gs, decay, step_size, h);
+      *reinterpret_cast<float4*>(P + i) = p4;
+      *reinterpret_cast<float4*>(M + i) = m4;
+      *reinterpret_cast<float4*>(Vv + i) = v4;
+      if (s.p16)
+        *reinterpret_cast<uint2*>(s.p16 + i) = make_uint2(pack_bf16x2(p4.x, p4.y), pack_bf16x2(p4.z, p4.w));
+    }
+  }
+  for (int64_t i = vec_end + threadIdx.x; i < end; i += blockDim.x) {
     float g = s.g_f32 ? reinterpret_cast<const float*>(s.g)[i]
                       : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(s.g)[i]);
-    g *= gs;
-    float p = s.p[i] * decay;
-    const float m = h.beta1 * s.m[i] + (1.f - h.beta1) * g;
-    const float v = h.beta2 * s.v[i] + (1.f - h.beta2) * g * g;
-    const float denom = sqrtf(v) / h.bc2_sqrt + h.eps;
-    p -= step_size * m / denom;
-    s.p[i] = p;
-    s.m[i] = m;
-    s.v[i] = v;
+    float p = P[i], m = M[i], v = Vv[i];
+    adam_elem(p, m, v, g * gs, decay, step_size, h);
+    P[i] = p;
+    M[i] = m;
+    Vv[i] = v;
     if (s.p16) s.p16[i] = __float2bfloat16_rn(p);
   }
 }
@@ -359,6 +397,10 @@ void adamw_multi(const std::vector<torch::Tensor>& params, const std::vector<tor
                       : nullptr;
     segs[i].n = params[i].numel();
     segs[i].wd = static_cast<float>(wds[i]);
+    auto al = [](const void* q, uintptr_t a) { return (reinterpret_cast<uintptr_t>(q) & (a - 1)) == 0; };
+    segs[i].pad = (al(segs[i].p, 16) && al(segs[i].m, 16) && al(segs[i].v, 16) &&
+                   al(segs[i].g, segs[i].g_f32 ? 16 : 8) && (!segs[i].p16 || al(segs[i].p16, 8)))
+                      ? 1 : 0;
     lens[i] = segs[i].n;
   }
   const c10::cuda::CUDAGuard g(params[0].device());
@@ -371,7 +413,7 @@ void adamw_multi(const std::vector<torch::Tensor>& params, const std::vector<tor
   constexpr int CH = 1 << 16;
   launch_chunked<AdamSeg>(segs, lens, CH, params[0].device(),
                           [&](const AdamSeg* s, const int2* c, const int64_t* o, int nc) {
-                            adamw_kernel<<<nc, 512, 0, st>>>(s, c, o, h, gsp, CH);
+                            adamw_kernel<<<nc, 256, 0, st>>>(s, c, o, h, gsp, CH);
                           });
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

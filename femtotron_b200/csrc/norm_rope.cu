@@ -83,13 +83,17 @@ __global__ void __launch_bounds__(NT) rmsnorm_fwd_kernel(const __nv_bfloat16* __
 }
 
 // dx = rstd * (dn - n * mean(dn * n)),  dn = dy * w,  n = x * rstd
-// dw += sum_rows dy * bf16(n)   (fp32 atomics into dw_acc[H])
+// dw += sum_rows dy * bf16(n)   (per-thread column partials, one 16-byte fp32 atomic per
+// 4 columns at the end of the block)
+// Each block walks a contiguous run of rows; the next row's x / dy vectors are loaded into
+// registers before the current row's block reduction, so HBM latency overlaps the reduction
+// and the dx stores instead of serialising with them.
 template <int NT, int VPT>
 __global__ void __launch_bounds__(NT) rmsnorm_bwd_kernel(
     const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x,
     const __nv_bfloat16* __restrict__ w, const float* __restrict__ rstd,
     __nv_bfloat16* __restrict__ dx, float* __restrict__ dw_acc, int T, int H, int64_t ldx,
-    int64_t lddy, int64_t lddx, int rows_per_block) {
+    int64_t lddy, int64_t lddx, int rows_per_block, int dw_vec) {
   __shared__ float red[NT / 32];
   float dwp[VPT][8];
 #pragma unroll
@@ -104,16 +108,39 @@ __global__ void __launch_bounds__(NT) rmsnorm_bwd_kernel(
   }
   const int r0 = blockIdx.x * rows_per_block;
   const int r1 = min(T, r0 + rows_per_block);
+  uint4 xq[VPT], gq[VPT];   // raw bf16 vectors of the row being processed
+  auto fetch = [&](int row) {
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int c = (threadIdx.x + i * NT) * 8;
+      if (c < H && row < r1) {
+        xq[i] = *reinterpret_cast<const uint4*>(x + (int64_t)row * ldx + c);
+        gq[i] = *reinterpret_cast<const uint4*>(dy + (int64_t)row * lddy + c);
+      }
+    }
+  };
+  auto unpack8 = [](const uint4& q, float* v) {
+    float2 f;
+    f = unpack_bf16x2(q.x); v[0] = f.x; v[1] = f.y;
+    f = unpack_bf16x2(q.y); v[2] = f.x; v[3] = f.y;
+    f = unpack_bf16x2(q.z); v[4] = f.x; v[5] = f.y;
+    f = unpack_bf16x2(q.w); v[6] = f.x; v[7] = f.y;
+  };
+  if (r0 < r1) fetch(r0);
   for (int row = r0; row < r1; ++row) {
     const float rs = rstd[row];
     float xv[VPT][8], gv[VPT][8];
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      unpack8(xq[i], xv[i]);
+      unpack8(gq[i], gv[i]);
+    }
+    fetch(row + 1);  // in flight during the reduction below
     float dot = 0.f;
 #pragma unroll
     for (int i = 0; i < VPT; ++i) {
       const int c = (threadIdx.x + i * NT) * 8;
       if (c < H) {
-        load8(x + (int64_t)row * ldx + c, xv[i]);
-        load8(dy + (int64_t)row * lddy + c, gv[i]);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const float n = xv[i][j] * rs;
@@ -138,12 +165,21 @@ __global__ void __launch_bounds__(NT) rmsnorm_bwd_kernel(
       }
     }
   }
+  if (r0 >= r1) return;
 #pragma unroll
   for (int i = 0; i < VPT; ++i) {
     const int c = (threadIdx.x + i * NT) * 8;
-    if (c < H)
+    if (c < H) {
+      if (dw_vec) {
+        atomicAdd(reinterpret_cast<float4*>(dw_acc + c),
+                  make_float4(dwp[i][0], dwp[i][1], dwp[i][2], dwp[i][3]));
+        atomicAdd(reinterpret_cast<float4*>(dw_acc + c + 4),
+                  make_float4(dwp[i][4], dwp[i][5], dwp[i][6], dwp[i][7]));
+      } else {
 #pragma unroll
-      for (int j = 0; j < 8; ++j) atomicAdd(dw_acc + c + j, dwp[i][j]);
+        for (int j = 0; j < 8; ++j) atomicAdd(dw_acc + c + j, dwp[i][j]);
+      }
+    }
   }
 }
 
@@ -281,21 +317,26 @@ void rmsnorm_bwd(const torch::Tensor& dy, const torch::Tensor& x, const torch::T
   int dev, sms;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int blocks = std::min(T, sms * 4);
-  const int rpb = (T + blocks - 1) / blocks;
-  const int nb = (T + rpb - 1) / rpb;
   auto a = reinterpret_cast<const __nv_bfloat16*>(dy.data_ptr());
   auto b = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr());
   auto c = reinterpret_cast<const __nv_bfloat16*>(w.data_ptr());
   auto d = reinterpret_cast<__nv_bfloat16*>(dx.data_ptr());
-#define FT_RMS_BWD(VPT)                                                                        \
-  rmsnorm_bwd_kernel<256, VPT><<<nb, 256, 0, st>>>(a, b, c, rstd.data_ptr<float>(), d,          \
+  const int dw_vec = (reinterpret_cast<uintptr_t>(dw_acc.data_ptr()) & 15) == 0 ? 1 : 0;
+  // one 8-wide vector per thread up to H = 8192 (wider blocks instead of more registers per
+  // thread, so two or more blocks stay resident per SM); about four blocks per SM in the grid
+#define FT_RMS_BWD(NT, VPT)                                                                      \
+  do {                                                                                         \
+    const int blocks = std::min(T, sms * std::max(1, 4 * 256 / (NT)));                         \
+    const int rpb = (T + blocks - 1) / blocks;                                                 \
+    const int nb = (T + rpb - 1) / rpb;                                                        \
+    rmsnorm_bwd_kernel<NT, VPT><<<nb, NT, 0, st>>>(a, b, c, rstd.data_ptr<float>(), d,         \
                                                    dw_acc.data_ptr<float>(), T, H, x.stride(0), \
-                                                   dy.stride(0), dx.stride(0), rpb)
-  if (H <= 2048) FT_RMS_BWD(1);
-  else if (H <= 4096) FT_RMS_BWD(2);
-  else if (H <= 8192) FT_RMS_BWD(4);
-  else FT_RMS_BWD(8);
+                                                   dy.stride(0), dx.stride(0), rpb, dw_vec);    \
+  } while (0)
+  if (H <= 2048) FT_RMS_BWD(256, 1);
+  else if (H <= 4096) FT_RMS_BWD(512, 1);
+  else if (H <= 8192) FT_RMS_BWD(1024, 1);
+  else FT_RMS_BWD(1024, 2);
 #undef FT_RMS_BWD
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

@@ -2,6 +2,7 @@
 
     python -m femtotron_b200.utils.kbench all            # every op, Llama-3-8B shapes
     python -m femtotron_b200.utils.kbench gemm_qkv --iters 20
+    python -m femtotron_b200.utils.kbench flash_fwd flash_fwd_v1 adamw   # several ops
     python -m femtotron_b200.utils.kbench flash_fwd --compare   # also time the torch library op
 
 Each op is timed with CUDA events on the launching stream after warm-up, with a synchronize
@@ -86,7 +87,7 @@ def op_gemm(name, M, N, K_, a_mn=False, b_mn=False, mode="store_bf16"):
     return {"kind": "flops", "flops": 2.0 * M * N * K_, "run": run, "lib": lib, "name": name}
 
 
-def op_flash(name, bwd: bool):
+def op_flash(name, bwd: bool, variant: int = 0):
     B, S = 1, T
     qkv = bf(B * S, (NQ + 2 * NKV) * D)
     o = torch.empty(B * S, NQ * D, device="cuda", dtype=torch.bfloat16)
@@ -98,7 +99,7 @@ def op_flash(name, bwd: bool):
     v = qkv[:, (NQ + NKV) * D:].view(B, S, NKV, D).transpose(1, 2)
     if not bwd:
         def run():
-            native().flash_fwd(qkv, o, lse, B, S, NQ, NKV, D, err)
+            native().flash_fwd_variant(qkv, o, lse, B, S, NQ, NKV, D, err, variant)
 
         def lib():
             F.scaled_dot_product_attention(q, k, v, is_causal=True, enable_gqa=True)
@@ -193,6 +194,11 @@ OPS = {
     "gemm_wgrad_gateup": lambda: op_gemm("gemm_wgrad_gateup", 2 * FF, H, T, a_mn=True, b_mn=True,
                                          mode="acc_f32"),
     "flash_fwd": lambda: op_flash("flash_fwd", False),
+    # forward variants: one query tile per CTA; two tiles reading S once (the default reads it
+    # twice); two tiles with a quarter of the exponentials on the FMA pipe
+    "flash_fwd_v1": lambda: op_flash("flash_fwd_v1", False, 1),
+    "flash_fwd_1pass": lambda: op_flash("flash_fwd_1pass", False, 3),
+    "flash_fwd_emu": lambda: op_flash("flash_fwd_emu", False, 4),
     "flash_bwd": lambda: op_flash("flash_bwd", True),
     "rmsnorm_fwd": lambda: op_rmsnorm("rmsnorm_fwd", False),
     "rmsnorm_bwd": lambda: op_rmsnorm("rmsnorm_bwd", True),
@@ -204,13 +210,14 @@ OPS = {
 
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    ap.add_argument("op", choices=sorted(OPS) + ["all"])
+    ap.add_argument("op", nargs="+", choices=sorted(OPS) + ["all"])
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--compare", action="store_true", help="also time the torch library op")
     args = ap.parse_args(argv)
     pk = peaks()
-    names = sorted(n for n in OPS if not n.startswith("p2p")) if args.op == "all" else [args.op]
+    names = (sorted(n for n in OPS if not n.startswith("p2p")) if "all" in args.op
+             else list(dict.fromkeys(args.op)))
     for n in names:
         spec = OPS[n]()
         flush = spec["kind"] == "flops"  # memory-bound ops already use inputs larger than L2

@@ -25,19 +25,45 @@ def ref_attention(qkv, B, S, nq, nkv, d):
     return o.transpose(1, 2).reshape(B * S, nq * d), lse
 
 
-@pytest.mark.parametrize("B,S,nq,nkv,d", [(2, 256, 4, 2, 64), (1, 512, 8, 2, 128), (2, 384, 4, 4, 128)])
-def test_flash_forward_matches_reference(B, S, nq, nkv, d):
+FWD_SHAPES = [(2, 256, 4, 2, 64), (1, 512, 8, 2, 128), (2, 384, 4, 4, 128), (1, 1024, 4, 1, 128)]
+
+
+# variant 1: one query tile per CTA; 2: two tiles (ping-pong), each row of S read twice from
+# TMEM (the default); 3: two tiles, S read once; 4: as 3 with a quarter of the exponentials on
+# the FMA pipe
+@pytest.mark.parametrize("variant", [1, 2, 3, 4])
+@pytest.mark.parametrize("B,S,nq,nkv,d", FWD_SHAPES)
+def test_flash_forward_matches_reference(B, S, nq, nkv, d, variant):
+    if variant != 1 and S % 256:
+        pytest.skip("the two-tile kernel pairs query blocks (S % 256 == 0)")
     torch.manual_seed(0)
     qkv = torch.randn(B * S, (nq + 2 * nkv) * d, device="cuda", dtype=torch.bfloat16)
     o = torch.empty(B * S, nq * d, device="cuda", dtype=torch.bfloat16)
     lse = torch.empty(B, nq, S, device="cuda", dtype=torch.float32)
-    native().flash_fwd(qkv, o, lse, B, S, nq, nkv, d, error_flag(qkv.device))
+    native().flash_fwd_variant(qkv, o, lse, B, S, nq, nkv, d, error_flag(qkv.device), variant)
     torch.cuda.synchronize()
     check_kernel_errors()
     ro, rl = ref_attention(qkv, B, S, nq, nkv, d)
     err = ((o.float() - ro).norm() / ro.norm()).item()
     assert err < 1e-2, err
     assert (lse - rl).abs().max().item() < 2e-2
+
+
+@pytest.mark.parametrize("variant", [1, 2, 3, 4])
+def test_flash_forward_large_scores(variant):
+    """Scores with a spread of tens of units push the running max up block after block, so
+    the lazily rescaled output accumulator is rescaled many times."""
+    B, S, nq, nkv, d = 1, 1024, 4, 2, 128
+    torch.manual_seed(3)
+    qkv = (3.0 * torch.randn(B * S, (nq + 2 * nkv) * d, device="cuda")).to(torch.bfloat16)
+    o = torch.empty(B * S, nq * d, device="cuda", dtype=torch.bfloat16)
+    lse = torch.empty(B, nq, S, device="cuda", dtype=torch.float32)
+    native().flash_fwd_variant(qkv, o, lse, B, S, nq, nkv, d, error_flag(qkv.device), variant)
+    torch.cuda.synchronize()
+    check_kernel_errors()
+    ro, rl = ref_attention(qkv, B, S, nq, nkv, d)
+    assert ((o.float() - ro).norm() / ro.norm()).item() < 1e-2
+    assert ((lse - rl).abs() / rl.abs().clamp_min(1.0)).max().item() < 1e-2
 
 
 @pytest.mark.parametrize("B,S,nq,nkv,d", [(2, 256, 4, 2, 64), (1, 512, 8, 2, 128), (2, 384, 4, 4, 128)])

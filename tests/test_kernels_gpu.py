@@ -104,7 +104,7 @@ def test_gemm_large_k_and_many_tiles():
     assert torch.equal(out, out2)
 
 
-@pytest.mark.parametrize("T,H", [(64, 256), (1000, 4096), (17, 5120)])
+@pytest.mark.parametrize("T,H", [(64, 256), (1000, 4096), (17, 5120), (9, 12288)])
 def test_rmsnorm(T, H):
     torch.manual_seed(6)
     x = torch.randn(T, H, device=DEV, dtype=torch.bfloat16)
@@ -189,6 +189,26 @@ def test_adamw_matches_torch():
     for p, rp, o in zip(ps, ref_p, outs):
         assert rel_err(p, rp.detach()) < 1e-5
         assert rel_err(o, rp.detach()) < 1e-2
+
+
+def test_adamw_fp32_grads_and_unaligned_views():
+    """fp32 gradients, and parameter / state views that start 4 bytes past a 16-byte boundary
+    (element-wise path) next to aligned ones (16-byte vector path)."""
+    torch.manual_seed(12)
+    base = [torch.randn(5003, device=DEV) for _ in range(3)]
+    ps = [base[0][1:2001], base[0][2004:5003], torch.randn(4099, device=DEV)]
+    ms = [torch.zeros(2001, device=DEV)[1:], torch.zeros(2999, device=DEV), torch.zeros(4099, device=DEV)]
+    vs = [torch.zeros(2001, device=DEV)[1:], torch.zeros(2999, device=DEV), torch.zeros(4099, device=DEV)]
+    gs = [torch.randn(p.numel(), device=DEV) for p in ps]
+    ref_p = [p.clone().requires_grad_(True) for p in ps]
+    opt = torch.optim.AdamW(ref_p, lr=1e-2, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1)
+    for step in range(1, 4):
+        for rp, g in zip(ref_p, gs):
+            rp.grad = g
+        opt.step()
+        K.adamw_multi(ps, ms, vs, gs, [], [0.1] * 3, lr=1e-2, beta1=0.9, beta2=0.95, eps=1e-8, step=step)
+    for p, rp in zip(ps, ref_p):
+        assert rel_err(p, rp.detach()) < 1e-5
 
 
 def test_sumsq_multi():
