@@ -44,7 +44,7 @@ void p2p_publish(const std::vector<int64_t>& flag_ptrs, int64_t rank, int64_t ep
 void p2p_reduce_scatter(const std::vector<int64_t>& buf_ptrs, int64_t flags_local,
                         const std::vector<int64_t>& flag_ptrs, torch::Tensor& acc, int64_t shard,
                         int64_t rank, int64_t epoch, double scale, bool accumulate,
-                        torch::Tensor& err, bool src_f32);
+                        torch::Tensor& err, bool src_f32, int64_t timeout_ms);
 void gemm_tc_fused(const torch::Tensor& A, const torch::Tensor& B, torch::Tensor& D, bool a_mn,
                    bool b_mn, int64_t mode,
                    const c10::optional<torch::Tensor>& R, const c10::optional<torch::Tensor>& GU,

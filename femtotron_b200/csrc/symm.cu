@@ -104,6 +104,7 @@ struct RSArgs {
   int world, rank, epoch, accumulate, wait;
   float scale;
   int* err;
+  uint64_t timeout_ns;           // bound of the flag wait
 };
 
 __device__ __forceinline__ uint64_t global_ns_() {
@@ -121,7 +122,8 @@ __global__ void p2p_publish_kernel(RSArgs a) {
   }
 }
 
-// Bounded wait (20 s: a peer that is that late has failed) for all peers' flags >= epoch.
+// Bounded wait for all peers' flags >= epoch (the caller's bound, 20 s by default: a peer
+// that is that late has failed).  On timeout: error code 100 + the first missing rank.
 __device__ __forceinline__ bool wait_peers(const RSArgs& a) {
   const uint64_t t0 = global_ns_();
   for (int r = 0; r < a.world; ++r) {
@@ -129,7 +131,7 @@ __device__ __forceinline__ bool wait_peers(const RSArgs& a) {
       int v;
       asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(a.flags_local + r) : "memory");
       if (v - a.epoch >= 0) break;
-      if (global_ns_() - t0 > 20000000000ull) {
+      if (global_ns_() - t0 > a.timeout_ns) {
         atomicExch(a.err, 100 + r);
         return false;
       }
@@ -228,7 +230,8 @@ void p2p_publish(const std::vector<int64_t>& flag_ptrs, int64_t rank, int64_t ep
 void p2p_reduce_scatter(const std::vector<int64_t>& buf_ptrs, int64_t flags_local,
                         const std::vector<int64_t>& flag_ptrs, torch::Tensor& acc, int64_t shard,
                         int64_t rank, int64_t epoch, double scale, bool accumulate,
-                        torch::Tensor& err, bool src_f32) {
+                        torch::Tensor& err, bool src_f32, int64_t timeout_ms) {
+  TORCH_CHECK(timeout_ms > 0, "p2p_reduce_scatter: timeout_ms must be positive");
   TORCH_CHECK(acc.scalar_type() == at::kFloat && acc.is_contiguous() && acc.numel() >= shard);
   TORCH_CHECK(shard % 8 == 0, "p2p_reduce_scatter: shard must be a multiple of 8 elements");
   RSArgs a = make_rs_args(buf_ptrs, flag_ptrs, rank, epoch);
@@ -243,6 +246,7 @@ void p2p_reduce_scatter(const std::vector<int64_t>& buf_ptrs, int64_t flags_loca
   a.accumulate = accumulate ? 1 : 0;
   a.scale = static_cast<float>(scale);
   a.err = err.data_ptr<int>();
+  a.timeout_ns = static_cast<uint64_t>(timeout_ms) * 1000000ull;
   int dev, sms;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);

@@ -27,6 +27,7 @@ from femtotron_b200.ops import functional as FN
 from femtotron_b200.ops.kernels import rope_tables
 from femtotron_b200.parallel.tensor_parallel import comm_ops as C
 from femtotron_b200.parallel.tensor_parallel.linear import ColumnParallelLinear, RowParallelLinear
+from femtotron_b200.utils.tracing import nvtx_range
 
 
 def _cfg(config, name, default=None):
@@ -274,8 +275,9 @@ class LlamaDecoderLayer(nn.Module):
             raise ValueError("LlamaDecoderLayer needs position_embeddings (cos, sin, pos)")
         if len(position_embeddings) == 2:
             position_embeddings = (position_embeddings[0], position_embeddings[1], None)
-        n = self.input_layernorm(x)
-        h = self.self_attn(n, position_embeddings, batch_shape, residual=x)
-        n2 = self.post_attention_layernorm(h)
-        out = self.mlp(n2, residual=h)
+        with nvtx_range(f"layer{self.layer_idx}"):
+            n = self.input_layernorm(x)
+            h = self.self_attn(n, position_embeddings, batch_shape, residual=x)
+            n2 = self.post_attention_layernorm(h)
+            out = self.mlp(n2, residual=h)
         return out.view(shape)

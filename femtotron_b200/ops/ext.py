@@ -12,9 +12,17 @@ import torch
 _C = None
 _IMPORT_ERROR: Exception | None = None
 
-# Number of native kernel launches issued through this module (one per entry-point call;
-# every entry point launches exactly one kernel).  Read by the benchmark.
+# Number of native kernel launches issued through this module.  Read by the benchmark.
 LAUNCHES = [0]
+
+# Kernels launched per call of an entry point when it is not exactly one: the flash backward
+# runs three (delta/LSE pre-pass, main, fp32 -> bf16 convert); the memory-management and
+# stream-memory-operation entry points launch none (copy engines, cuStreamWrite/WaitValue).
+KERNELS_PER_CALL = {
+    "flash_bwd": 3,
+    "symm_alloc": 0, "ipc_handle": 0, "ipc_open": 0, "ipc_close": 0, "tensor_at": 0,
+    "copy_from_ptrs": 0, "stream_wait_geq": 0, "stream_write": 0,
+}
 
 
 class _Counted:
@@ -27,9 +35,10 @@ class _Counted:
         fn = getattr(self._mod, name)
         if not callable(fn):
             return fn
+        n = KERNELS_PER_CALL.get(name, 1)
 
         def wrapped(*a, **k):
-            LAUNCHES[0] += 1
+            LAUNCHES[0] += n
             return fn(*a, **k)
         wrapped.__name__ = name
         return wrapped

@@ -40,6 +40,8 @@ import os
 # FT_ZERO3_DEBUG_NOCOPY=1 skips the parameter transfer of every gather (wrong numerics; used
 # only to separate the cost of the transfer from the cost of its bookkeeping)
 _DEBUG_NOCOPY = os.environ.get("FT_ZERO3_DEBUG_NOCOPY") == "1"
+# bound of the in-kernel wait for the peers' gradient flags (a peer that late has failed)
+P2P_TIMEOUT_MS = int(os.environ.get("FT_P2P_TIMEOUT_MS", "20000"))
 
 
 class ParamGroupCluster:
@@ -266,7 +268,7 @@ class ParamGroupCluster:
             if self.rs_mode == "p2p":
                 C.p2p_reduce_scatter([heap.peer_ptr(r, goff) for r in range(R)], flags[rank], flags,
                                      self.flat_grad_shard, self.shard_size, rank, ep, 1.0 / R,
-                                     accumulate, error_flag(self.device), f32)
+                                     accumulate, error_flag(self.device), f32, P2P_TIMEOUT_MS)
                 return
             nb = self.shard_size * (4 if f32 else 2)
             for r in range(R):                  # peers' flags, waited in the stream (no SMs)

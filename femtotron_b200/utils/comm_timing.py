@@ -15,6 +15,8 @@ from contextlib import contextmanager
 
 import torch
 
+from femtotron_b200.utils.tracing import PHASES, nvtx_range
+
 
 class CommWaitTimer:
     def __init__(self):
@@ -25,18 +27,22 @@ class CommWaitTimer:
     @contextmanager
     def wait(self, kind: str):
         if not self.enabled or not torch.cuda.is_available():
-            yield
+            with nvtx_range("wait:" + kind):
+                yield
             return
         a = torch.cuda.Event(enable_timing=True)
         a.record()
-        yield
+        with nvtx_range("wait:" + kind):
+            yield
         b = torch.cuda.Event(enable_timing=True)
         b.record()
         self._pending.append((kind, a, b))
 
     def mark(self, label: str | None) -> None:
         """Phase mark on the current stream: the device time until the next mark is added to
-        ``phase:<label>`` (label None only closes the previous phase)."""
+        ``phase:<label>`` (label None only closes the previous phase).  The same marks
+        delimit NVTX ranges when FT_NVTX=1."""
+        PHASES.switch(None if label is None else "phase:" + label)
         if not self.enabled or not torch.cuda.is_available():
             return
         e = torch.cuda.Event(enable_timing=True)

@@ -108,8 +108,25 @@ def w_tp_model(rank, world, sequence_parallel):
 
 
 # ----------------------------------------------------------------------------- ZeRO 0..3
+def _inject_delays(model, seed, max_s=0.02):
+    """Host-side random sleeps before every decoder layer's forward and backward on this
+    rank: the ranks reach their collectives (ZeRO gathers / reduce-scatters) at shifted
+    times, which shakes out ordering assumptions between ranks."""
+    import random
+    import time
+    from femtotron_b200.models.layers import LlamaDecoderLayer
+    rng = random.Random(seed)
+
+    def nap(*_):
+        time.sleep(rng.uniform(0.0, max_s))
+    for mod in model.modules():
+        if isinstance(mod, LlamaDecoderLayer):
+            mod.register_forward_pre_hook(nap)
+            mod.register_full_backward_pre_hook(nap)
+
+
 def _train(cfg, sd, ctx, stage, steps, mb, ga, seed_data, lr=5e-3, clip=None, ckpt=None,
-           resume=None, ac=False):
+           resume=None, ac=False, delay_seed=None):
     from femtotron_b200.data import DistributedDataLoader, SyntheticTokens, simple_pretrain_collator
     from femtotron_b200.models import build_llama_model, get_llama_parallel_plan, materialize_model
     from femtotron_b200.parallel.data_parallel import create_grad_synchronizer
@@ -122,6 +139,8 @@ def _train(cfg, sd, ctx, stage, steps, mb, ga, seed_data, lr=5e-3, clip=None, ck
     m = build_llama_model(cfg, ctx)
     materialize_model(m, "cpu", dtype=torch.float32, init_std=None)
     load_sharded(m, sd, ctx)
+    if delay_seed is not None:
+        _inject_delays(m, delay_seed)
     tc = TrainConfig(train_steps=steps, grad_accum_steps=ga, master_dtype=torch.float32,
                      param_dtype=torch.float32, log_interval=10 ** 6,
                      checkpoint_interval=ckpt[1] if ckpt else 10 ** 6,
@@ -148,6 +167,18 @@ def w_zero(rank, world, stage, ac):
     sd = full_state(cfg)
     ctx = ctx_of(dp=world)
     losses = _train(cfg, sd, ctx, stage, steps=4, mb=2, ga=2, seed_data=3, ac=ac)
+    t = torch.tensor(losses)
+    dist.all_reduce(t)
+    return (t / world).tolist()
+
+
+def w_zero_delayed(rank, world, stage):
+    """Same run as w_zero with random host delays on rank 1 only."""
+    cfg = tiny_config()
+    sd = full_state(cfg)
+    ctx = ctx_of(dp=world)
+    losses = _train(cfg, sd, ctx, stage, steps=4, mb=2, ga=2, seed_data=3,
+                    delay_seed=100 + rank if rank == 1 else None)
     t = torch.tensor(losses)
     dist.all_reduce(t)
     return (t / world).tolist()

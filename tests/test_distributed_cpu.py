@@ -39,6 +39,15 @@ def test_zero_stages_agree():
     assert base[-1] < base[0]
 
 
+@pytest.mark.parametrize("stage", [2, 3])
+def test_random_host_delays_do_not_change_results(stage):
+    """Delay injection: one rank sleeps a random time before each layer's forward and
+    backward; the loss curve must equal the undelayed run's."""
+    a = run_ranks(W.w_zero_delayed, 2, stage)[0]
+    b = run_ranks(W.w_zero, 2, stage, False)[0]
+    assert max(abs(x - y) for x, y in zip(a, b)) < 1e-6, (a, b)
+
+
 def test_zero3_with_activation_checkpointing_agrees():
     a = run_ranks(W.w_zero, 2, 3, True)[0]
     b = run_ranks(W.w_zero, 2, 3, False)[0]

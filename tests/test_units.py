@@ -176,3 +176,16 @@ def test_policy_from_config():
     assert pol(nn.ReLU()) and not pol(nn.Linear(1, 1))
     with pytest.raises(ValueError):
         policy_from_config({"type": "bogus"})
+
+
+def test_nvtx_helpers_are_noops_when_disabled():
+    from femtotron_b200.utils import tracing
+    from femtotron_b200.utils.comm_timing import TIMER
+    with tracing.nvtx_range("x"):
+        pass
+    tracing.PHASES.switch("phase:a")
+    tracing.PHASES.switch(None)
+    with TIMER.wait("k"):
+        pass
+    TIMER.mark("fwd")
+    TIMER.mark(None)
