@@ -354,6 +354,16 @@ FT_DEVICE float2 unpack_bf16x2(uint32_t v) {
   return __bfloat1622float2(b);
 }
 
+// Debug builds (FT_KERNEL_CHECKS=1 in the environment of `setup.py build_ext`): FT_DCHECK(cond,
+// err, code) records `code` in the kernel's status word when `cond` is false and evaluates to
+// false so the caller skips the access; in release builds it is the constant true.  The host
+// reads the status word with check_kernel_errors() like a bounded-wait timeout.
+#ifdef FT_KERNEL_CHECKS
+#define FT_DCHECK(cond, err, code) ((cond) ? true : ((err) ? (atomicExch((err), (code)), false) : false))
+#else
+#define FT_DCHECK(cond, err, code) true
+#endif
+
 // 2^x by one special-function-unit instruction (ex2.approx.ftz; 2^-inf = 0, subnormal results
 // flush to zero, which the softmax probabilities that use it never need).
 FT_DEVICE float ex2_approx(float x) {

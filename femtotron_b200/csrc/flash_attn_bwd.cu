@@ -18,15 +18,17 @@
 //   warp 9     MMA issuer (also owns TMEM):
 //                dP^T = V dO_i^T     (TMEM dP, lanes = keys, columns = queries)
 //                S^T  = K Q_i^T      (TMEM S)
-//                dV  += P^T dO_i     (A = P^T from shared memory, B = dO MN-major)
+//                dV  += P^T dO_i     (A = P^T from TMEM, packed bf16 over the S columns,
+//                                    B = dO MN-major)
 //                dK  += dS^T Q_i     (A = dS^T, B = Q MN-major)
 //                dQ_i = dS K         (A = the same dS^T tile read MN-major, B = K MN-major),
-//                                    written into the S columns, which are free by then
+//                                    written into the S columns after the dV product
 //   warps 0-7  compute: two warps per TMEM lane quadrant (32 keys), each owning 64 of the
 //              128 query columns: P^T = exp2(S^T * scale*log2e - lse2), causal mask on the
-//              diagonal block, dS^T = P^T * (dP^T - delta); both to shared memory as bf16
-//              128-byte-swizzled tiles; then dQ_i out of TMEM into fp32 staging boxes and a
-//              bulk reduce-add to global memory; finally dV and dK the same way.
+//              diagonal block, written back into TMEM as packed bf16; dS^T = P^T * (dP^T -
+//              delta) to shared memory as a bf16 128-byte-swizzled tile; then dQ_i out of TMEM
+//              into fp32 staging boxes and a bulk reduce-add to global memory; finally dV and
+//              dK the same way.
 // TMEM columns: S/dQ [0,128), dP [128,256), dV [256, 256+D), dK [256+D, 256+2D).
 // All waits are bounded (2 s): on timeout the kernel records an error code and leaves.
 //
@@ -84,7 +86,7 @@ struct Smem {
   __nv_bfloat16 v[BKV * D];
   __nv_bfloat16 q[BQ * D];
   __nv_bfloat16 dout[BQ * D];
-  __nv_bfloat16 p[BKV * BQ];   // P^T (rows = keys); also fp32 staging for dQ/dK/dV
+  __nv_bfloat16 p[BKV * BQ];   // fp32 staging boxes for dQ/dK/dV (P^T itself stays in TMEM)
   __nv_bfloat16 ds[BKV * BQ];  // dS^T (rows = keys); also fp32 staging
   float lse2[BQ];
   float delta[BQ];
@@ -195,7 +197,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       constexpr uint32_t idKV = make_idesc_bf16(128, D, false, true);   // P^T/dS^T x (dO|Q)
       constexpr uint32_t idQ = make_idesc_bf16(128, D, true, true);     // dS (MN-major) x K
       const uint32_t ka = smem_u32(s.k), va = smem_u32(s.v), qa = smem_u32(s.q);
-      const uint32_t doa = smem_u32(s.dout), pa = smem_u32(s.p), dsa = smem_u32(s.ds);
+      const uint32_t doa = smem_u32(s.dout), dsa = smem_u32(s.ds);
       bool ok = wait_b(&s.kv_full, 0, p.err, 43);
       for (int it = 0; it < niter && ok; ++it) {
         const uint32_t par = it & 1;
@@ -220,17 +222,20 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                    idS, kk > 0 ? 1u : 0u);
         }
         mma_commit(&s.s_full);
-        // dV += P^T dO
+        // dV += P^T dO, A = P^T from TMEM: packed bf16 pairs of queries 0..63 in S columns
+        // 0..31 and of queries 64..127 in columns 64..95 (8 columns per 16 queries)
         if (!wait_b(&s.p_full, par, p.err, 47)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < BQ / 16; ++kk) {
-          const uint64_t ad = make_sw128_desc(pa + (kk >> 2) * 128 * 128 + (kk & 3) * 32, 16, 1024);
+          const uint32_t at = tS + (kk >> 2) * 64 + (kk & 3) * 8;
           const uint64_t bd = make_sw128_desc(doa + kk * 2048, 128 * 128, 1024);
-          mma_bf16(tdV, ad, bd, idKV, (it > 0 || kk > 0) ? 1u : 0u);
+          mma_bf16_ts(tdV, at, bd, idKV, (it > 0 || kk > 0) ? 1u : 0u);
         }
         mma_commit(&s.do_empty);
-        // dK += dS^T Q, then dQ = dS K into the S columns
+        // dK += dS^T Q, then dQ = dS K into the S columns (the dV product above, which reads
+        // P^T from those columns, was issued earlier, and tcgen05.mma operations of one
+        // thread execute in order)
         if (!wait_b(&s.ds_full, par, p.err, 48)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll
@@ -257,10 +262,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     const int r = quad * 32 + lane;  // key row within the block (TMEM lane)
     const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
     const int col0 = half * (BQ / 2);  // this thread's 64 query columns
-    // fp32 staging boxes of this warp: the 4 KB it owns in the P tile and in the dS tile
+    // fp32 staging boxes of this warp: the 4 KB it owns in the staging tile and in the dS tile
     float* box0 = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(s.p) + half * 16384 + quad * 4096);
     float* box1 = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(s.ds) + half * 16384 + quad * 4096);
-    uint8_t* prow = reinterpret_cast<uint8_t*>(s.p) + half * 128 * 128 + r * 128;
     uint8_t* dsrow = reinterpret_cast<uint8_t*>(s.ds) + half * 128 * 128 + r * 128;
     bool ok = true;
     for (int it = 0; it < niter && ok; ++it) {
@@ -291,23 +295,25 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             if (col0 + c < r) pv[c] = 0.f;
         }
       }
+      // P^T as packed bf16 pairs into the first 32 of this warp's 64 S columns (all of which
+      // this warp has read): the dV product takes it from TMEM
+#pragma unroll
+      for (int h16 = 0; h16 < 2; ++h16) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int c = 0; c < 16; ++c) pk[c] = pack_bf16x2(pv[32 * h16 + 2 * c], pv[32 * h16 + 2 * c + 1]);
+        tmem_st_32x32b_x16(tS + lane_off + col0 + 16 * h16, pk);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s.p_full);
       // the staging boxes (inside the P and dS tiles) must have been read by the bulk
       // reductions of the previous block before they are overwritten
       if (it > 0) {
         if (lane == 0) tma_store_wait_read();
         __syncwarp();
       }
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int pos = (u ^ (r & 7)) * 16;
-        *reinterpret_cast<uint4*>(prow + pos) =
-            make_uint4(pack_bf16x2(pv[8 * u], pv[8 * u + 1]), pack_bf16x2(pv[8 * u + 2], pv[8 * u + 3]),
-                       pack_bf16x2(pv[8 * u + 4], pv[8 * u + 5]), pack_bf16x2(pv[8 * u + 6], pv[8 * u + 7]));
-      }
-      fence_proxy_async_smem();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&s.p_full);
       // ---- dS^T = P^T * (dP^T - delta)
       if (!wait_b(&s.dp_full, par, p.err, 50)) { ok = false; break; }
       tc_fence_after();

@@ -190,6 +190,7 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t tmem_acc
               __nv_bfloat16* d;
               if (p.mode == EPI_SCATTER_BF16) {
                 const int owner = row / p.scatter_rows;
+                if (!FT_DCHECK(owner < 8 && p.scatter_base[owner] != nullptr, p.err, 90)) continue;
                 d = p.scatter_base[owner] + (int64_t)(row - owner * p.scatter_rows) * p.ldd + col0;
               } else {
                 d = reinterpret_cast<__nv_bfloat16*>(p.D) + (int64_t)row * p.ldd + col0;

@@ -175,6 +175,7 @@ __global__ void p2p_reduce_scatter_kernel(RSArgs a) {
 #pragma unroll
     for (int r = 0; r < 8; ++r) {
       if (r >= a.world) break;
+      if (!FT_DCHECK(a.bufs[r] != nullptr, a.err, 91)) break;
       float f[8];
       load8(a.bufs[r], base + v * 8, f, F32);
 #pragma unroll

@@ -20,6 +20,10 @@ NVCC_FLAGS = [
     "-DNDEBUG",
 ]
 
+# FT_KERNEL_CHECKS=1: compile the in-kernel debug checks (FT_DCHECK in common.cuh)
+if os.environ.get("FT_KERNEL_CHECKS") == "1":
+    NVCC_FLAGS.append("-DFT_KERNEL_CHECKS")
+
 sources = sorted(glob.glob(os.path.join(CSRC, "*.cu"))) + sorted(glob.glob(os.path.join(CSRC, "*.cpp")))
 
 setup(
