@@ -96,12 +96,8 @@ def model_config(layers=None, config="llama3-8b-zero3"):
 def flops_per_token(cfg, seq) -> float:
     """Model FLOPs per trained token: 6 x (matmul parameters) + 6 x L x H x S for causal
     attention (score and value products, forward+backward).  Recomputation is not counted."""
-    H, L, V = cfg.hidden_size, cfg.num_hidden_layers, cfg.vocab_size
-    d = H // cfg.num_attention_heads
-    kv = cfg.num_key_value_heads * d
-    per_layer = H * H + 2 * H * kv + H * H + 3 * H * cfg.intermediate_size
-    n_matmul = L * per_layer + V * H
-    return 6.0 * n_matmul + 6.0 * L * H * seq
+    from femtotron_b200.utils.flops import llama_flops_per_token
+    return llama_flops_per_token(cfg, seq)
 
 
 def peaks():

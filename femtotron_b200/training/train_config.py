@@ -35,3 +35,4 @@ class TrainConfig:
     warmup_steps: int = 50
     min_lr_ratio: float = 0.1
     metrics_path: str | None = None      # JSONL metrics per logged step (rank 0)
+    peak_tflops: float | None = None     # per-GPU bf16 peak for MFU (None: B200 dense 2250)

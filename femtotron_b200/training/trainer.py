@@ -5,8 +5,10 @@ deferred with ``no_sync`` on all but the last) or one pipeline-runner step, then
 synchronisation, ``MixedPrecisionManager.step()`` and the LR scheduler.
 
 Additions over the reference:
-  * step time measured with CUDA events and reduced as the max over ranks (``step_ms``),
-    tokens/s for the whole job, and JSONL metrics (``TrainConfig.metrics_path``);
+  * step time measured with CUDA events and reduced as the max over ranks at log steps
+    (``step_ms_max``), tokens/s for the whole job (host clock and device clock), MFU, the
+    compute stream's time blocked on communication (FT_COMM_TIMING=1), peak memory, and JSONL
+    metrics (``TrainConfig.metrics_path``);
   * the loss stays on the device until the end of the step (one device->host read);
   * optional NaN/Inf abort, kernel bounded-wait error check at log intervals;
   * checkpoints keep the reference layout (``step_N/meta.json``, ``shard_tp{t}_dp{d}.pt``,
@@ -153,7 +155,30 @@ class Trainer:
         return total / n
 
     # ------------------------------------------------------------------ logging
+    def _reduce_max(self, values: list[float]) -> list[float]:
+        """Element-wise max over all ranks (every rank calls this at the same steps)."""
+        if not (dist.is_available() and dist.is_initialized()):
+            return values
+        dev = self.device if dist.get_backend() == "nccl" else torch.device("cpu")
+        t = torch.tensor(values, dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return t.tolist()
+
     def _log_step(self, info: dict):
+        """Called on every rank at log intervals: reduces the step time (and, with
+        FT_COMM_TIMING=1, the compute stream's time blocked on communication) as the max over
+        ranks, checks the native kernels' status words, then rank 0 prints and appends the
+        JSONL record."""
+        from femtotron_b200.utils.comm_timing import TIMER
+        from femtotron_b200.utils.flops import B200_BF16_DENSE_TFLOPS, llama_flops_per_token
+        blocked = None
+        if TIMER.enabled and self.device.type == "cuda":
+            waits = {k: v for k, v in TIMER.collect().items() if not k.startswith("phase:")}
+            blocked = sum(waits.values())
+        step_ms, blocked_max = self._reduce_max([info["step_ms"], blocked or 0.0])
+        if self.device.type == "cuda":
+            from femtotron_b200.ops.ext import check_kernel_errors
+            check_kernel_errors(self.device)
         if _rank() != 0:
             return
         now = time.perf_counter()
@@ -163,21 +188,38 @@ class Trainer:
             tps = tok * (self.global_step - self._last_log_step) / (now - self._last_log_time)
         self._last_log_time, self._last_log_step = now, self.global_step
         mem = torch.cuda.max_memory_allocated() / 2 ** 30 if self.device.type == "cuda" else 0.0
+        rec = dict(info, step_ms_max=step_ms, tokens_per_s=tps, peak_mem_gb=mem, time=time.time())
+        if tok and step_ms > 0:
+            rec["tokens_per_s_device"] = tok / (step_ms / 1e3)
+            cfg = getattr(self.model, "config", None)
+            seq = self._seq_len()
+            if cfg is not None and seq:
+                peak = self.train_config.peak_tflops or B200_BF16_DENSE_TFLOPS
+                world = dist.get_world_size() if dist.is_available() and dist.is_initialized() else 1
+                rec["mfu"] = rec["tokens_per_s_device"] * llama_flops_per_token(cfg, seq) / (world * peak * 1e12)
+                rec["mfu_peak_tflops"] = peak
+        if blocked is not None:
+            rec["comm_blocked_ms_max"] = blocked_max
+            rec["comm_blocked_frac"] = blocked_max / step_ms if step_ms > 0 else float("nan")
         msg = (f"step {self.global_step:>6}/{self.train_config.train_steps} | loss {info['loss']:7.4f} | "
-               f"lr {info['lr']:.2e} | tok/s {tps:>9.0f} | step {info['step_ms']:.1f} ms | mem {mem:.1f}GB")
+               f"lr {info['lr']:.2e} | tok/s {tps:>9.0f} | step {step_ms:.1f} ms | mem {mem:.1f}GB")
+        if "mfu" in rec:
+            msg += f" | mfu {rec['mfu']:.3f}"
         if "grad_norm" in info:
             msg += f" | gnorm {info['grad_norm']:.3f}"
         print(msg, flush=True)
         path = getattr(self.train_config, "metrics_path", None)
         if path:
-            rec = dict(info, tokens_per_s=tps, peak_mem_gb=mem, time=time.time())
             with open(path, "a") as f:
                 f.write(json.dumps(rec) + "\n")
 
-    def tokens_per_step(self) -> int:
+    def _seq_len(self) -> int:
         ds = getattr(self.dataloader, "dataset", None)
-        seq = ds.shape[1] if ds is not None and hasattr(ds, "shape") else 0
-        return self.dataloader.micro_batch_size * seq * self.train_config.grad_accum_steps * self.parallel_ctx.dp_size
+        return int(ds.shape[1]) if ds is not None and hasattr(ds, "shape") else 0
+
+    def tokens_per_step(self) -> int:
+        return (self.dataloader.micro_batch_size * self._seq_len() * self.train_config.grad_accum_steps
+                * self.parallel_ctx.dp_size)
 
     # ------------------------------------------------------------------ checkpoints
     def _shard_name(self) -> str:

@@ -19,9 +19,17 @@ def test_cli_tp2_then_verify(tmp_path):
     cfg = os.path.join(ROOT, "configs", "tiny_llama_debug.yaml")
     common = ["--config", cfg, "--num_hidden_layers", "2", "--seq_len", "64", "--micro_batch_size", "2",
               "--checkpoint_dir", str(tmp_path / "ck")]
-    out = _run(common + ["--train_steps", "4", "--checkpoint_interval", "4", "--zero_stage", "3"], tmp_path)
+    metrics = tmp_path / "metrics.jsonl"
+    out = _run(common + ["--train_steps", "4", "--checkpoint_interval", "4", "--zero_stage", "3",
+                         "--log_interval", "2", "--metrics_path", str(metrics)], tmp_path)
     assert out.returncode == 0, out.stdout[-2000:] + out.stderr[-3000:]
     assert "step      4/4" in out.stdout
+    import json
+    recs = [json.loads(l) for l in metrics.read_text().splitlines()]
+    assert [r["step"] for r in recs] == [2, 4]
+    for key in ("loss", "lr", "step_ms_max", "tokens_per_s_device", "mfu", "peak_mem_gb"):
+        assert key in recs[-1], (key, recs[-1])
+    assert recs[-1]["step_ms_max"] >= recs[-1]["step_ms"] > 0
     assert os.path.isfile(tmp_path / "ck" / "step_4" / "_SUCCESS")
     out = _run(common + ["--zero_stage", "3", "--resume", str(tmp_path / "ck" / "step_4")], tmp_path,
                module="femtotron_b200.scripts.verify_training")
