@@ -182,6 +182,62 @@ def op_p2p_copy(name, streams: int):
     return {"kind": "bytes", "bytes": n * 2, "run": run, "name": name}
 
 
+# ---- fused communication kernels, emulated on one GPU: every "peer" buffer is a local one
+# and every flag is already published, so the kernels run their full code path (flag checks,
+# per-owner addressing) against local HBM instead of NVLink.  Shapes: Llama-2-13B with TP=8 and
+# sequence parallelism (micro-batch 2, seq 4096) and one Llama-3-8B ZeRO-3 unit at DP=8.
+TP, T13, H13, QKV13 = 8, 2 * 4096, 5120, 3 * 5120 // 8
+
+
+def op_gemm_gated(name):
+    """All-gather -> GEMM: the QKV projection whose A rows (the sequence-parallel activations)
+    arrive in TP chunks; the producer checks chunk flags before each A tile."""
+    from femtotron_b200.parallel.tensor_parallel.fused import fused_gemm
+    a, b = bf(T13, H13), bf(QKV13, H13)
+    out = torch.empty(T13, QKV13, device="cuda", dtype=torch.bfloat16)
+    flags = torch.ones(TP, dtype=torch.int32, device="cuda")
+    gate = dict(gate_flags=flags.data_ptr(), gate_op=1, gate_epoch=1, gate_off=0,
+                gate_row_elems=H13, gate_chunk_elems=(T13 // TP) * H13)
+
+    def run():
+        fused_gemm(a, b, out, gate=gate)
+    return {"kind": "flops", "flops": 2.0 * T13 * QKV13 * H13, "run": run, "name": name}
+
+
+def op_gemm_scatter(name):
+    """GEMM -> reduce-scatter: the o_proj partial product whose rows are stored straight into
+    their owner rank's slot (here TP local slots)."""
+    from femtotron_b200.parallel.tensor_parallel.fused import fused_gemm
+    k = H13 // TP
+    a, b = bf(T13, k), bf(H13, k)
+    out = torch.empty(T13, H13, device="cuda", dtype=torch.bfloat16)
+    slots = torch.empty(TP, T13 // TP, H13, device="cuda", dtype=torch.bfloat16)
+    ptrs = [slots[r].data_ptr() for r in range(TP)]
+
+    def run():
+        fused_gemm(a, b, out, scatter=(ptrs, T13 // TP))
+    return {"kind": "flops", "flops": 2.0 * T13 * H13 * k, "run": run, "name": name}
+
+
+def op_rs_p2p(name):
+    """ZeRO-3 gradient reduce-scatter with the fp32 cast, 1/dp scale and accumulation fused:
+    one Llama-3-8B unit (218 M parameters, fp32 gradients) at DP=8, this rank's slice."""
+    from femtotron_b200.ops.ext import error_flag
+    R, shard = 8, 218 * 1000 * 1000 // 8 // 8 * 8
+    # rank 0 reads elements [0, shard) of every peer's buffer: allocate only that slice
+    bufs = [torch.randn(shard, device="cuda") for _ in range(R)]
+    flags = torch.ones(R, dtype=torch.int32, device="cuda")
+    acc = torch.zeros(shard, device="cuda")
+    err = error_flag(acc.device)
+    ptrs = [b.data_ptr() for b in bufs]
+
+    def run():
+        native().p2p_reduce_scatter(ptrs, flags.data_ptr(), [flags.data_ptr()] * R, acc, shard, 0, 1,
+                                    1.0 / R, True, err, True, 2000)
+    # read R slices + the accumulator, write the accumulator (fp32)
+    return {"kind": "bytes", "bytes": shard * 4 * (R + 2), "run": run, "name": name}
+
+
 OPS = {
     "p2p_copy_1": lambda: op_p2p_copy("p2p_copy_1", 1),
     "p2p_copy_4": lambda: op_p2p_copy("p2p_copy_4", 4),
@@ -204,6 +260,9 @@ OPS = {
     "rmsnorm_bwd": lambda: op_rmsnorm("rmsnorm_bwd", True),
     "swiglu_fwd": lambda: op_swiglu("swiglu_fwd"),
     "adamw": lambda: op_adamw("adamw"),
+    "gemm_gated_ag": lambda: op_gemm_gated("gemm_gated_ag"),
+    "gemm_scatter_rs": lambda: op_gemm_scatter("gemm_scatter_rs"),
+    "rs_p2p": lambda: op_rs_p2p("rs_p2p"),
     "xent_stats": lambda: op_xent("xent_stats"),
 }
 
