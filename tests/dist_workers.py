@@ -125,8 +125,8 @@ def _inject_delays(model, seed, max_s=0.02):
             mod.register_full_backward_pre_hook(nap)
 
 
-def _train(cfg, sd, ctx, stage, steps, mb, ga, seed_data, lr=5e-3, clip=None, ckpt=None,
-           resume=None, ac=False, delay_seed=None):
+def _build_trainer(cfg, sd, ctx, stage, steps, mb, ga, seed_data, lr=5e-3, clip=None, ckpt=None,
+                   ac=False, delay_seed=None, check_finite=False):
     from femtotron_b200.data import DistributedDataLoader, SyntheticTokens, simple_pretrain_collator
     from femtotron_b200.models import build_llama_model, get_llama_parallel_plan, materialize_model
     from femtotron_b200.parallel.data_parallel import create_grad_synchronizer
@@ -155,7 +155,14 @@ def _train(cfg, sd, ctx, stage, steps, mb, ga, seed_data, lr=5e-3, clip=None, ck
     sch = create_lr_schedule(mp.inner, 1, steps)
     ds = SyntheticTokens(64, 32, cfg.vocab_size, seed=seed_data)
     dl = DistributedDataLoader(ds, ctx, mb, simple_pretrain_collator, num_workers=0, pin_memory=False)
-    tr = Trainer(m, mp, sch, dl, create_grad_synchronizer(mp.groups, ctx, st), ctx, tc)
+    return Trainer(m, mp, sch, dl, create_grad_synchronizer(mp.groups, ctx, st), ctx, tc,
+                   check_finite=check_finite)
+
+
+def _train(cfg, sd, ctx, stage, steps, mb, ga, seed_data, lr=5e-3, clip=None, ckpt=None,
+           resume=None, ac=False, delay_seed=None):
+    tr = _build_trainer(cfg, sd, ctx, stage, steps, mb, ga, seed_data, lr=lr, clip=clip, ckpt=ckpt,
+                        ac=ac, delay_seed=delay_seed)
     if resume:
         tr._load_checkpoint(resume)
     hist = tr.train()
@@ -241,6 +248,85 @@ def w_pipeline(rank, world, schedule):
 
 
 # ----------------------------------------------------------------------------- faults
+def w_failure_modes(rank, world, tmpdir):
+    """Host-side fault injection on gloo ranks:
+    * an exception inside a ZeRO-3 unit's forward, recovered by force_reshard_all, after which
+      training continues exactly as an undisturbed run;
+    * a checkpoint without its _SUCCESS marker, and one whose shard file is truncated: both
+      refuse to load;
+    * a NaN in a parameter: the trainer's finite-loss check aborts the step on every rank."""
+    from femtotron_b200.models.layers import LlamaDecoderLayer
+    cfg = tiny_config()
+    sd = full_state(cfg)
+    ctx = ctx_of(dp=world)
+    out = {}
+    # -- exception inside a unit, then recovery
+    clean = _build_trainer(cfg, sd, ctx, 3, steps=2, mb=2, ga=1, seed_data=9)
+    clean.dataloader.set_epoch(0)
+    ref = clean.train_step(iter(clean.dataloader))["loss"]
+    tr = _build_trainer(cfg, sd, ctx, 3, steps=2, mb=2, ga=1, seed_data=9)
+    layer = [m for m in tr.model.modules() if isinstance(m, LlamaDecoderLayer)][1]
+    fired = []
+
+    def boom(*_):
+        if not fired:
+            fired.append(1)
+            raise RuntimeError("injected failure inside a ZeRO-3 unit")
+    h = layer.register_forward_pre_hook(boom)
+    tr.dataloader.set_epoch(0)
+    try:
+        tr.train_step(iter(tr.dataloader))
+        out["raised"] = False
+    except RuntimeError as e:
+        out["raised"] = "injected" in str(e)
+    h.remove()
+    tr.mp_manager.strategy.force_reshard_all()
+    out["all_resharded"] = all(c._full_buffer is None and c._prefetch is None
+                               for c in tr.mp_manager.strategy.clusters)
+    tr.dataloader.set_epoch(0)
+    out["recovered_loss_matches"] = abs(tr.train_step(iter(tr.dataloader))["loss"] - ref) < 1e-6
+    # -- incomplete checkpoints
+    ck = os.path.join(tmpdir, "ck")
+    tr.train_config.checkpoint_dir = ck
+    tr.global_step = 1
+    d = tr._save_checkpoint()
+    dist.barrier()
+    if rank == 0:
+        os.remove(os.path.join(d, "_SUCCESS"))
+    dist.barrier()
+    try:
+        tr._load_checkpoint(d)
+        out["missing_success_refused"] = False
+    except RuntimeError as e:
+        out["missing_success_refused"] = "_SUCCESS" in str(e)
+    dist.barrier()
+    if rank == 0:
+        with open(os.path.join(d, "_SUCCESS"), "w") as f:
+            f.write("ok")
+    shard = os.path.join(d, tr._shard_name())
+    with open(shard, "r+b") as f:
+        f.truncate(max(1, os.path.getsize(shard) // 2))
+    dist.barrier()
+    try:
+        tr._load_checkpoint(d)
+        out["truncated_refused"] = False
+    except Exception:
+        out["truncated_refused"] = True
+    dist.barrier()
+    # -- NaN abort
+    nan_tr = _build_trainer(cfg, sd, ctx, 3, steps=2, mb=2, ga=1, seed_data=9, check_finite=True)
+    with torch.no_grad():
+        emb = nan_tr.model.model.embed_tokens.weight
+        emb.fill_(float("nan"))
+    nan_tr.dataloader.set_epoch(0)
+    try:
+        nan_tr.train_step(iter(nan_tr.dataloader))
+        out["nan_aborted"] = False
+    except FloatingPointError:
+        out["nan_aborted"] = True
+    return out
+
+
 def w_rank_failure(rank, world):
     """Rank 1 dies between steps; rank 0's next collective must fail with an error (process
     group timeout), not hang."""

@@ -75,6 +75,11 @@ def test_pipeline_matches_single_rank(schedule):
         assert r["worst"] < 1e-4, r
 
 
+def test_failure_injection_on_the_host(tmp_path):
+    for r in run_ranks(W.w_failure_modes, 2, str(tmp_path)):
+        assert all(r.values()), r
+
+
 def test_rank_leaving_makes_peers_fail_fast():
     res = run_ranks(W.w_rank_failure, 2, pg_timeout=5.0, timeout=120.0)
     assert res[1] == {"left": True}
