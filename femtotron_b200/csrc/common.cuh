@@ -354,6 +354,20 @@ FT_DEVICE float2 unpack_bf16x2(uint32_t v) {
   return __bfloat1622float2(b);
 }
 
+// Raise a kernel's dynamic shared-memory limit once per device: the attribute belongs to the
+// device's context, so a process that drives several GPUs must set it on each.  `done` is one
+// bit per device ordinal (a static of the caller, one per kernel instance).
+template <typename Kernel>
+inline void smem_attr_once(Kernel kernel, int bytes, unsigned long long& done) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (!(done & bit)) {
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    done |= bit;
+  }
+}
+
 // Debug builds (FT_KERNEL_CHECKS=1 in the environment of `setup.py build_ext`): FT_DCHECK(cond,
 // err, code) records `code` in the kernel's status word when `cond` is false and evaluates to
 // false so the caller skips the access; in release builds it is the constant true.  The host

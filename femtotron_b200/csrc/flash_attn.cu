@@ -744,12 +744,8 @@ void flash_fwd_variant(const torch::Tensor& qkv, torch::Tensor& o, torch::Tensor
 #define FT_FA_PP(DD, EE, OP)                                                                    \
     do {                                                                                       \
       const int smem = sizeof(fa2::Smem<DD>) + 1024;                                           \
-      static bool cfg = false;                                                                 \
-      if (!cfg) {                                                                              \
-        cudaFuncSetAttribute(fa2::flash_fwd_pp_kernel<DD, EE, OP>,                             \
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, smem);              \
-        cfg = true;                                                                            \
-      }                                                                                        \
+      static unsigned long long cfg = 0;                                                       \
+      smem_attr_once(fa2::flash_fwd_pp_kernel<DD, EE, OP>, smem, cfg);                         \
       fa2::flash_fwd_pp_kernel<DD, EE, OP><<<grid, fa2::NTHREADS, smem, st>>>(tm, p);         \
     } while (0)
     if (D == 128) {
@@ -768,13 +764,13 @@ void flash_fwd_variant(const torch::Tensor& qkv, torch::Tensor& o, torch::Tensor
   dim3 grid(B * nq, S / 128);
   if (D == 128) {
     const int smem = sizeof(Smem<128>) + 1024;
-    static bool cfg = false;
-    if (!cfg) { cudaFuncSetAttribute(flash_fwd_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem); cfg = true; }
+    static unsigned long long cfg = 0;
+    smem_attr_once(flash_fwd_kernel<128>, smem, cfg);
     flash_fwd_kernel<128><<<grid, NTHREADS, smem, st>>>(tm, p);
   } else {
     const int smem = sizeof(Smem<64>) + 1024;
-    static bool cfg = false;
-    if (!cfg) { cudaFuncSetAttribute(flash_fwd_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem); cfg = true; }
+    static unsigned long long cfg = 0;
+    smem_attr_once(flash_fwd_kernel<64>, smem, cfg);
     flash_fwd_kernel<64><<<grid, NTHREADS, smem, st>>>(tm, p);
   }
   C10_CUDA_KERNEL_LAUNCH_CHECK();

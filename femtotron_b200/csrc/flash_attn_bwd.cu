@@ -457,11 +457,8 @@ template <int D>
 void launch_main(const CUtensorMap& tq, const CUtensorMap& td, const CUtensorMap& ta, const Params& p,
                  dim3 grid, cudaStream_t st) {
   const int smem = sizeof(Smem<D>) + 1024;
-  static bool cfg = false;
-  if (!cfg) {
-    cudaFuncSetAttribute(flash_bwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    cfg = true;
-  }
+  static unsigned long long cfg = 0;
+  smem_attr_once(flash_bwd_kernel<D>, smem, cfg);
   flash_bwd_kernel<D><<<grid, NTHREADS, smem, st>>>(tq, td, ta, p);
 }
 

@@ -664,11 +664,8 @@ static void launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p
                    cudaStream_t stream) {
   auto kern = gemm_kernel<A_MN, B_MN, BN, STAGES>;
   const int smem = static_cast<int>(sizeof(Smem<BN, STAGES>)) + 1024;
-  static bool configured = false;  // one flag per template instance
-  if (!configured) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    configured = true;
-  }
+  static unsigned long long configured = 0;  // per device, one mask per template instance
+  smem_attr_once(kern, smem, configured);
   const int grid = std::max(1, std::min(num_tiles, num_sms()));
   kern<<<grid, NUM_THREADS, smem, stream>>>(ta, tb, p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
@@ -680,11 +677,8 @@ static void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUte
   constexpr int STAGES = PBN == 256 ? 6 : 7;
   auto kern = gemm_pair_kernel<A_MN, B_MN, PBN, STAGES>;
   const int smem = static_cast<int>(sizeof(PairSmem<PBN, STAGES>)) + 1024;
-  static bool configured = false;
-  if (!configured) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    configured = true;
-  }
+  static unsigned long long configured = 0;  // per device, one mask per template instance
+  smem_attr_once(kern, smem, configured);
   const int pairs = std::max(1, std::min(num_tiles, num_sms() / 2));
   kern<<<2 * pairs, NUM_THREADS, smem, stream>>>(ta, tb, td, p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();

@@ -201,7 +201,8 @@ def op_gemm_gated(name):
 
     def run():
         fused_gemm(a, b, out, gate=gate)
-    return {"kind": "flops", "flops": 2.0 * T13 * QKV13 * H13, "run": run, "name": name}
+    # `keep` holds the flag tensor alive: the kernel only receives its address
+    return {"kind": "flops", "flops": 2.0 * T13 * QKV13 * H13, "run": run, "name": name, "keep": flags}
 
 
 def op_gemm_scatter(name):
@@ -216,7 +217,7 @@ def op_gemm_scatter(name):
 
     def run():
         fused_gemm(a, b, out, scatter=(ptrs, T13 // TP))
-    return {"kind": "flops", "flops": 2.0 * T13 * H13 * k, "run": run, "name": name}
+    return {"kind": "flops", "flops": 2.0 * T13 * H13 * k, "run": run, "name": name, "keep": slots}
 
 
 def op_rs_p2p(name):
@@ -234,6 +235,7 @@ def op_rs_p2p(name):
     def run():
         native().p2p_reduce_scatter(ptrs, flags.data_ptr(), [flags.data_ptr()] * R, acc, shard, 0, 1,
                                     1.0 / R, True, err, True, 2000)
+    run.keep = bufs   # the peer buffers are passed by address only
     # read R slices + the accumulator, write the accumulator (fp32)
     return {"kind": "bytes", "bytes": shard * 4 * (R + 2), "run": run, "name": name}
 
