@@ -87,6 +87,9 @@ class Trainer:
 
     def train_step(self, data_iter) -> dict:
         """One optimizer step; returns {loss, lr, successful, step_ms, grad_norm?}."""
+        # idempotent: registers the strategy's backward hooks (ZeRO-2) on first use, so a
+        # caller driving train_step directly gets the same gradients as train()
+        self.mp_manager.strategy.prepare_for_backward(self.mp_manager.groups)
         timed = self.device.type == "cuda"
         if timed:
             ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)

@@ -342,3 +342,164 @@ def w_rank_failure(rank, world):
     except Exception as e:  # gloo raises on timeout / peer loss
         return {"raised": True, "elapsed": time.time() - t0, "msg": str(e)[:100]}
     return {"raised": False}
+
+
+# ----------------------------------------------------------------------------- model loading
+def w_model_loading(rank, world, tmpdir):
+    """Reference test_model_loading: rank 0 writes an HF LlamaForCausalLM with save_pretrained
+    (safetensors), every rank loads its TP slices with ModelLoader; the sharded model's loss and
+    its weight-gradient slices must match the HF model's."""
+    from transformers import LlamaForCausalLM
+    from femtotron_b200.models import build_llama_model, materialize_model
+    from femtotron_b200.models.model_loader import ModelLoader, shard_for_rank
+    from femtotron_b200.models.parallel_plan import get_llama_parallel_plan
+    cfg = tiny_config()
+    torch.manual_seed(11)
+    hf = LlamaForCausalLM(cfg).float()
+    path = os.path.join(tmpdir, "hf")
+    if rank == 0:
+        hf.save_pretrained(path, safe_serialization=True)
+    dist.barrier()
+    ctx = ctx_of(tp=world)
+    m = build_llama_model(cfg, ctx)
+    materialize_model(m, "cpu", dtype=torch.float32, init_std=0.02)
+    ModelLoader(ctx).load_and_distribute(m, path, device="cpu")
+    ids = torch.randint(0, cfg.vocab_size, (2, 32), generator=torch.Generator().manual_seed(3))
+    loss = m(input_ids=ids, labels=ids)["loss"]
+    loss.backward()
+    ref = hf(input_ids=ids, labels=ids).loss
+    ref.backward()
+    plan = get_llama_parallel_plan()
+    hfp = dict(hf.named_parameters())
+    worst_w = worst_g = 0.0
+    for name, p in m.named_parameters():
+        key = name.replace("._checkpoint_wrapped_module", "")
+        w_ref = shard_for_rank(hfp[key].detach(), key, plan, ctx.tp_rank, ctx.tp_size)
+        g_ref = shard_for_rank(hfp[key].grad, key, plan, ctx.tp_rank, ctx.tp_size)
+        worst_w = max(worst_w, (p.detach() - w_ref).abs().max().item())
+        g = p.main_grad if getattr(p, "main_grad", None) is not None else p.grad
+        worst_g = max(worst_g, ((g - g_ref).norm() / (g_ref.norm() + 1e-12)).item())
+    return {"loss": loss.item(), "ref": ref.item(), "worst_w": worst_w, "worst_g": worst_g}
+
+
+# ----------------------------------------------------------------------------- DP x TP splits
+def _global_batches(cfg, steps, gb, seq=32, seed=21):
+    g = torch.Generator().manual_seed(seed)
+    return [torch.randint(0, cfg.vocab_size, (gb, seq), generator=g) for _ in range(steps)]
+
+
+def _run_split(cfg, sd, ctx, stage, steps, mb, ga, seed=21):
+    """Train `steps` optimizer steps where global step s consumes the fixed global batch G_s
+    (dp x ga x mb rows): DP rank r, micro-batch k takes rows [(r*ga + k)*mb, ... + mb).
+    Returns the loss curve averaged over all ranks (= the global-batch mean)."""
+    gb = ctx.dp_size * ga * mb
+    batches = _global_batches(cfg, steps, gb, seed=seed)
+    tr = _build_trainer(cfg, sd, ctx, stage, steps=steps, mb=mb, ga=ga, seed_data=1)
+    r = ctx.dp_rank
+    losses = []
+    for s in range(steps):
+        def it(s=s):
+            for k in range(ga):
+                x = batches[s][(r * ga + k) * mb:(r * ga + k + 1) * mb]
+                yield {"input_ids": x, "labels": x}
+        losses.append(tr.train_step(it())["loss"])
+    t = torch.tensor(losses, dtype=torch.float64)
+    dist.all_reduce(t)
+    return (t / dist.get_world_size()).tolist()
+
+
+def w_dp_tp_split(rank, world, dp, tp, stage):
+    """Reference test_dp_training: the same global batches under every legal (DP, TP) split."""
+    cfg = tiny_config(num_key_value_heads=4)
+    sd = full_state(cfg)
+    return _run_split(cfg, sd, ctx_of(dp=dp, tp=tp), stage, steps=3, mb=8 // dp, ga=1)
+
+
+def w_grad_accum(rank, world, mb, ga):
+    """Reference test_gradient_accum: (micro-batch, accumulation) pairs with the same global
+    batch give the same loss curve."""
+    cfg = tiny_config()
+    sd = full_state(cfg)
+    return _run_split(cfg, sd, ctx_of(dp=world), 1, steps=3, mb=mb, ga=ga)
+
+
+# ----------------------------------------------------------------------------- pipeline stage
+def w_stage_errors(rank, world):
+    """Reference test_pipeline_stage (error handling / state management) on a one-stage
+    pipeline (first and last): out-of-order calls raise with the micro-batch id, leftover
+    state is reported by assert_clean, reset recovers, and a full micro-batch matches a direct
+    forward/backward of the model."""
+    from femtotron_b200.models import build_llama_model, materialize_model
+    from femtotron_b200.parallel.pipeline_parallel import PipelineStage
+    cfg = tiny_config()
+    ctx = ctx_of(pp=1)
+    m = build_llama_model(cfg, ctx, use_pp_aware=True, layer_range=range(cfg.num_hidden_layers))
+    materialize_model(m, "cpu", dtype=torch.float32, init_std=0.02)
+    st = PipelineStage(m, ctx, loss_scale=0.5)
+    ids = torch.randint(0, cfg.vocab_size, (2, 16), generator=torch.Generator().manual_seed(2))
+    out = {}
+
+    def raises(fn, text):
+        try:
+            fn()
+        except RuntimeError as e:
+            return text in str(e)
+        return False
+    out["forward_without_input"] = raises(lambda: st.forward(0), "forward(0): no input staged")
+    out["backward_without_output"] = raises(lambda: st.backward(3), "backward(3): no output")
+    st.stage_input(0, ids)
+    out["double_input"] = raises(lambda: st.stage_input(0, ids), "input already staged")
+    out["forward_without_labels"] = raises(lambda: st.forward(0), "last stage requires labels")
+    st.stage_labels(0, ids)
+    out["leftover_reported"] = raises(st.assert_clean, "leftover per-microbatch state")
+    st.reset()
+    st.assert_clean()
+    out["reset_clean"] = True
+    # one micro-batch through the stage == direct loss * loss_scale, same gradients
+    st.stage_input(1, ids)
+    st.stage_labels(1, ids)
+    st.forward(1)
+    out["double_forward"] = raises(lambda: st.forward(1), "output already exists")
+    st.backward(1)
+    loss = st.pop_all_losses()[1].item()
+    st.assert_clean()
+
+    def grad_of(p):
+        return p.main_grad if getattr(p, "main_grad", None) is not None else p.grad
+    g_stage = {n: grad_of(p).clone() for n, p in m.named_parameters()}
+    for p in m.parameters():
+        p.grad = None
+        if getattr(p, "main_grad", None) is not None:
+            p.main_grad.zero_()
+    ref = m(ids, labels=ids)["loss"] * 0.5
+    ref.backward()
+    out["loss_matches"] = abs(loss - ref.item()) < 1e-6
+    out["grads_match"] = all(torch.allclose(g_stage[n], grad_of(p), atol=1e-6, rtol=1e-5)
+                             for n, p in m.named_parameters())
+    return out
+
+
+# ----------------------------------------------------------------------------- clipping
+def w_clip_norm_vs_torch(rank, world, tp):
+    """Reference test_mixed_precision (clipping): the global gradient norm that ClipGradNorm
+    reports equals torch.nn.utils.clip_grad_norm_'s total norm of the same gradients, for
+    DP-replicated (ZeRO-0), DP-sharded (ZeRO-1/2/3, including ZeRO-3's unsharded free
+    parameters) and TP-sharded gradients."""
+    cfg = tiny_config()
+    sd = full_state(cfg)
+    dp = world // tp
+    x = _global_batches(cfg, 1, 4 * dp, seed=5)[0]
+    out = {}
+    for stage in (0, 1, 2, 3):
+        ctx = ctx_of(dp=dp, tp=tp)
+        tr = _build_trainer(cfg, sd, ctx, stage, steps=1, mb=4, ga=1, seed_data=1, clip=0.05)
+        r = ctx.dp_rank
+        mine = x[r * 4:(r + 1) * 4]
+        info = tr.train_step(iter([{"input_ids": mine, "labels": mine}]))
+        out[f"zero{stage}"] = info["grad_norm"]
+    # reference: one process, the same batches (mean of the DP ranks' losses)
+    ref = _single_model(cfg, sd)
+    loss = sum(ref(x[r * 4:(r + 1) * 4], labels=x[r * 4:(r + 1) * 4])["loss"] for r in range(dp)) / dp
+    loss.backward()
+    out["torch"] = torch.nn.utils.clip_grad_norm_(list(ref.parameters()), max_norm=1e9).item()
+    return out

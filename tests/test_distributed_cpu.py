@@ -31,6 +31,42 @@ def test_tp_model_matches_single_process(sp):
         assert r["worst"] < 1e-4, r
 
 
+@pytest.mark.parametrize("world", [1, 2])
+def test_model_loading_from_hf_safetensors(world, tmp_path):
+    for r in run_ranks(W.w_model_loading, world, str(tmp_path)):
+        assert r["worst_w"] == 0.0, r
+        assert abs(r["loss"] - r["ref"]) < 1e-4, r
+        assert r["worst_g"] < 1e-3, r
+
+
+def test_dp_tp_splits_agree():
+    """Same global batches under (dp, tp) = (4, 1), (2, 2), (1, 4) on four ranks."""
+    curves = {(dp, tp): run_ranks(W.w_dp_tp_split, 4, dp, tp, 0)[0] for dp, tp in ((4, 1), (2, 2), (1, 4))}
+    base = curves[(4, 1)]
+    for k, c in curves.items():
+        assert max(abs(a - b) for a, b in zip(c, base)) < 1e-4, (k, c, base)
+    assert base[-1] < base[0]
+
+
+def test_gradient_accumulation_splits_agree():
+    curves = {(mb, ga): run_ranks(W.w_grad_accum, 2, mb, ga)[0] for mb, ga in ((4, 1), (2, 2), (1, 4))}
+    base = curves[(4, 1)]
+    for k, c in curves.items():
+        assert max(abs(a - b) for a, b in zip(c, base)) < 1e-4, (k, c, base)
+
+
+@pytest.mark.parametrize("tp", [1, 2])
+def test_grad_norm_matches_torch_clip_grad_norm(tp):
+    for r in run_ranks(W.w_clip_norm_vs_torch, 2, tp):
+        for stage in range(4):
+            assert abs(r[f"zero{stage}"] - r["torch"]) < 1e-4 * r["torch"], (stage, r)
+
+
+def test_pipeline_stage_call_order_and_state():
+    r = run_ranks(W.w_stage_errors, 1)[0]
+    assert all(r.values()), r
+
+
 def test_zero_stages_agree():
     curves = {s: run_ranks(W.w_zero, 2, s, False)[0] for s in (0, 1, 2, 3)}
     base = curves[0]
