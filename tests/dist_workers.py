@@ -503,3 +503,77 @@ def w_clip_norm_vs_torch(rank, world, tp):
     loss.backward()
     out["torch"] = torch.nn.utils.clip_grad_norm_(list(ref.parameters()), max_norm=1e9).item()
     return out
+
+
+# ----------------------------------------------------------------------------- reference parity
+def _load_reference(ref_root):
+    import sys
+    if ref_root not in sys.path:
+        sys.path.insert(0, ref_root)
+    from femtotron.parallel_context import ParallelContext as RCtx
+    from femtotron.model.llama import build_llama_model as rbuild
+    return RCtx, rbuild
+
+
+def w_reference_parity(rank, world, ref_root, steps):
+    """BASELINE configuration 1 against the reference's own modules on the same gloo ranks:
+    tiny LLaMA (4 layers, hidden 256, 8/4 heads, FFN 688, vocab 2048), TP=2, fp32, seq 128,
+    micro-batch 4, uniform token ids from seed 0, identical initial weights.  Both sides run
+    forward + backward of their own model and an identical AdamW update of the full
+    parameters, so the loss curves must agree."""
+    from collections import OrderedDict
+    from transformers import LlamaConfig
+    from femtotron_b200.models import build_llama_model, materialize_model
+    from femtotron_b200.models.model_loader import shard_for_rank
+    from femtotron_b200.models.parallel_plan import get_llama_parallel_plan
+    RCtx, rbuild = _load_reference(ref_root)
+    cfg = LlamaConfig(hidden_size=256, intermediate_size=688, num_attention_heads=8,
+                      num_key_value_heads=4, num_hidden_layers=4, vocab_size=2048,
+                      max_position_embeddings=512, rms_norm_eps=1e-5, rope_theta=10000.0,
+                      tie_word_embeddings=False, attn_implementation="sdpa")
+    cfg.use_cache = False
+    sd = full_state(cfg)
+    plan = get_llama_parallel_plan()
+    g = torch.Generator().manual_seed(0)
+    batches = [torch.randint(0, 2048, (4, 128), generator=g) for _ in range(steps)]
+
+    ctx = ctx_of(tp=world)
+    ours = build_llama_model(cfg, ctx)
+    materialize_model(ours, "cpu", dtype=torch.float32, init_std=None)
+    load_sharded(ours, sd, ctx)
+
+    rctx = RCtx(OrderedDict([("pp", 1), ("dp", 1), ("tp", world)]))
+    ref = rbuild(cfg, rctx).to_empty(device="cpu")
+    with torch.no_grad():
+        for name, p in ref.named_parameters():
+            p.copy_(shard_for_rank(sd[name], name, plan, rctx.tp_rank, rctx.tp_size))
+        rot = ref.model.rotary_emb   # the reference's own tests recompute inv_freq after to_empty
+        d = cfg.hidden_size // cfg.num_attention_heads
+        theta = (getattr(cfg, "rope_parameters", None) or {}).get("rope_theta", 10000.0)
+        inv = 1.0 / (theta ** (torch.arange(0, d, 2, dtype=torch.float32) / d))
+        rot.inv_freq.copy_(inv)
+        if hasattr(rot, "original_inv_freq"):
+            rot.original_inv_freq.copy_(inv)
+
+    def run(model, grad_of):
+        opt = torch.optim.AdamW(list(model.parameters()), lr=3e-4, betas=(0.9, 0.95), eps=1e-8,
+                                weight_decay=0.0)
+        losses = []
+        for x in batches:
+            opt.zero_grad(set_to_none=True)
+            for p in model.parameters():
+                if getattr(p, "main_grad", None) is not None:
+                    p.main_grad.zero_()
+            loss = model(x, labels=x)["loss"]
+            loss.backward()
+            for p in model.parameters():
+                gr = grad_of(p)
+                if gr is not p.grad:
+                    p.grad = gr.clone()
+            opt.step()
+            losses.append(loss.item())
+        return losses
+
+    mine = run(ours, lambda p: p.main_grad if getattr(p, "main_grad", None) is not None else p.grad)
+    theirs = run(ref, lambda p: p.grad)
+    return {"ours": mine, "reference": theirs}

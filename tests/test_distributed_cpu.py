@@ -67,6 +67,18 @@ def test_pipeline_stage_call_order_and_state():
     assert all(r.values()), r
 
 
+def test_tiny_tp2_matches_reference_modules():
+    """BASELINE configuration 1 with the reference's own code as the oracle (skipped when the
+    reference is not installed under baseline/_ref)."""
+    import os
+    ref_root = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref_root, "femtotron")):
+        pytest.skip("reference not installed under baseline/_ref")
+    for r in run_ranks(W.w_reference_parity, 2, ref_root, 10, timeout=600.0):
+        assert len(r["ours"]) == 10
+        assert max(abs(a - b) for a, b in zip(r["ours"], r["reference"])) < 1e-4, r
+
+
 def test_zero_stages_agree():
     curves = {s: run_ranks(W.w_zero, 2, s, False)[0] for s in (0, 1, 2, 3)}
     base = curves[0]

@@ -189,3 +189,31 @@ def test_nvtx_helpers_are_noops_when_disabled():
         pass
     TIMER.mark("fwd")
     TIMER.mark(None)
+
+
+def test_saved_tensor_log_diff_and_activation_checkpointing():
+    import torch
+    from common_models import tiny_config
+    from femtotron_b200.models import LlamaForTraining, materialize_model
+    from femtotron_b200.models.layers import LlamaDecoderLayer
+    from femtotron_b200.training import apply_activation_checkpointing
+    from femtotron_b200.training.ckpt_policy import by_class
+    from femtotron_b200.utils.saved_tensors import SavedTensorLog, diff_saved, format_diff
+    cfg = tiny_config()
+    with torch.device("meta"):
+        m = LlamaForTraining(cfg)
+    materialize_model(m, "cpu", dtype=torch.float32, init_std=0.02)
+    ids = torch.randint(0, cfg.vocab_size, (2, 32), generator=torch.Generator().manual_seed(0))
+    logs = []
+    for name in ("first", "second"):   # same call site: locations compare equal
+        with SavedTensorLog(name) as log:
+            m(ids, labels=ids)["loss"]
+        logs.append(log)
+    a, b = logs
+    assert len(a.entries) > 0 and format_diff(diff_saved(a, b)) == "saved tensors agree"
+    apply_activation_checkpointing(m, by_class(LlamaDecoderLayer), use_reentrant=False)
+    with SavedTensorLog("ac") as c:
+        m(ids, labels=ids)["loss"].backward()
+    d = diff_saved(a, c)
+    assert d["only_a"] and c.saved_bytes < a.saved_bytes, (a.summary(), c.summary())
+    assert "only in a:" in format_diff(d)
