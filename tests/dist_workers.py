@@ -577,3 +577,78 @@ def w_reference_parity(rank, world, ref_root, steps):
     mine = run(ours, lambda p: p.main_grad if getattr(p, "main_grad", None) is not None else p.grad)
     theirs = run(ref, lambda p: p.grad)
     return {"ours": mine, "reference": theirs}
+
+
+def w_reference_zero_parity(rank, world, ref_root, stage, steps):
+    """Full-framework parity with the reference on CPU gloo ranks: the reference's own
+    MixedPrecisionManager (ZeRO `stage`, torch AdamW), LR schedule, parameter groups and
+    Trainer step against this package's, on the same weights and the same per-rank batches
+    (DP=world, fp32 compute and master weights)."""
+    from collections import OrderedDict
+    from femtotron_b200.models.model_loader import shard_for_rank
+    from femtotron_b200.models.parallel_plan import get_llama_parallel_plan
+    RCtx, rbuild = _load_reference(ref_root)
+    from femtotron.model.parallel_plan import get_llama_parallel_plan as rplan
+    from femtotron.training.train_config import TrainConfig as RTC
+    from femtotron.training.optimizer import get_param_groups as rgroups
+    from femtotron.training.mixed_precision_manager import MixedPrecisionManager as RMP
+    from femtotron.training.lr_schedule import create_lr_schedule as rlr
+    from femtotron.sharding.factory import create_sharding_strategy as rstrat
+    from femtotron.sharding.zero_config import ZeROConfig as RZ
+    from femtotron.scripts.presets import get_wrap_policy
+    from femtotron.parallel.data_parallel.gradient_synchronizer import create_grad_synchronizer as rsync
+    cfg = tiny_config()
+    cfg.use_cache = False
+    sd = full_state(cfg)
+    batches = _global_batches(cfg, steps, 2 * world, seed=13)
+    mine = [b[rank * 2:(rank + 1) * 2] for b in batches]
+
+    def it():
+        for x in mine:
+            yield {"input_ids": x, "labels": x}
+
+    # ours: same hyper-parameters as _build_trainer (AdamW 5e-3, betas 0.9/0.95, wd 0.01,
+    # warm-up 1 step, cosine to 0.1)
+    tr = _build_trainer(cfg, sd, ctx_of(dp=world), stage, steps=steps, mb=2, ga=1, seed_data=1)
+    gi = it()
+    ours = [tr.train_step(gi)["loss"] for _ in range(steps)]
+
+    rctx = RCtx(OrderedDict([("pp", 1), ("dp", world), ("tp", 1)]))
+    ref = rbuild(cfg, rctx).to_empty(device="cpu")
+    plan = get_llama_parallel_plan()
+    with torch.no_grad():
+        for name, p in ref.named_parameters():
+            p.copy_(shard_for_rank(sd[name], name, plan, 0, 1))
+        rot = ref.model.rotary_emb
+        d = cfg.hidden_size // cfg.num_attention_heads
+        theta = (getattr(cfg, "rope_parameters", None) or {}).get("rope_theta", 10000.0)
+        inv = 1.0 / (theta ** (torch.arange(0, d, 2, dtype=torch.float32) / d))
+        rot.inv_freq.copy_(inv)
+        if hasattr(rot, "original_inv_freq"):
+            rot.original_inv_freq.copy_(inv)
+    tc = RTC(master_dtype=torch.float32, param_dtype=torch.float32, grad_clip=None,
+             train_steps=steps, log_interval=10 ** 6, checkpoint_interval=10 ** 6, warmup_steps=1,
+             min_lr_ratio=0.1, lr=5e-3)
+    wrap = get_wrap_policy("llama_decoder_layer") if stage == 3 else None
+    strategy = rstrat(rctx, RZ(stage=stage, wrap_policy=wrap))
+    mp = RMP(model=ref, sharding_strategy=strategy, parallel_ctx=rctx, parallel_plan=rplan(),
+             config=tc, inner_optimizer_cls=torch.optim.AdamW,
+             inner_optimizer_kwargs={"lr": 5e-3, "betas": (0.9, 0.95), "eps": 1e-8},
+             compute_param_groups=rgroups(ref, weight_decay=0.01))
+    sched = rlr(mp.inner, warmup_steps=1, total_steps=steps, min_lr_ratio=0.1)
+    gs = rsync(mp.groups, rctx, strategy)
+    mp.strategy.prepare_for_backward(mp.groups)
+    # the reference Trainer pins cuda:{current_device} in its constructor, so its standard
+    # step (femtotron/training/trainer.py:157-190, grad_accum_steps=1) is replayed here with
+    # its own components; the optimizer step runs under no_grad (ZeRO-1/2 weight gathers
+    # modify views in place, which autograd rejects on CPU)
+    theirs = []
+    for x in mine:
+        loss = ref(input_ids=x, labels=x)["loss"]
+        loss.backward()
+        gs.sync_gradients()
+        with torch.no_grad():
+            mp.step()
+        sched.step()
+        theirs.append(loss.item())
+    return {"ours": ours, "reference": theirs}

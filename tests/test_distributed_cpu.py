@@ -79,6 +79,18 @@ def test_tiny_tp2_matches_reference_modules():
         assert max(abs(a - b) for a, b in zip(r["ours"], r["reference"])) < 1e-4, r
 
 
+@pytest.mark.parametrize("stage", [0, 1, 2, 3])
+def test_zero_training_matches_reference_framework(stage):
+    """DP=2 training through the reference's own MixedPrecisionManager / ZeRO strategy / LR
+    schedule against this package's Trainer: same weights and batches, same loss curve."""
+    import os
+    ref_root = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref_root, "femtotron")):
+        pytest.skip("reference not installed under baseline/_ref")
+    for r in run_ranks(W.w_reference_zero_parity, 2, ref_root, stage, 4, timeout=600.0):
+        assert max(abs(a - b) for a, b in zip(r["ours"], r["reference"])) < 1e-4, r
+
+
 def test_zero_stages_agree():
     curves = {s: run_ranks(W.w_zero, 2, s, False)[0] for s in (0, 1, 2, 3)}
     base = curves[0]
