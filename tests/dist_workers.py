@@ -652,3 +652,41 @@ def w_reference_zero_parity(rank, world, ref_root, stage, steps):
         sched.step()
         theirs.append(loss.item())
     return {"ours": ours, "reference": theirs}
+
+
+def w_reference_state_dict_interchange(rank, world, ref_root):
+    """The model part of a checkpoint (HF parameter names, TP-sliced) is interchangeable with
+    the reference's: same keys and shapes per TP rank, and a state dict of this package's
+    model loads strictly into the reference model and reproduces its loss."""
+    from collections import OrderedDict
+    RCtx, rbuild = _load_reference(ref_root)
+    from femtotron_b200.models import build_llama_model, materialize_model
+    cfg = tiny_config()
+    cfg.use_cache = False
+    sd = full_state(cfg)
+    ctx = ctx_of(tp=world)
+    ours = build_llama_model(cfg, ctx)
+    materialize_model(ours, "cpu", dtype=torch.float32, init_std=None)
+    load_sharded(ours, sd, ctx)
+    rctx = RCtx(OrderedDict([("pp", 1), ("dp", 1), ("tp", world)]))
+    ref = rbuild(cfg, rctx).to_empty(device="cpu")
+    mine = {k: v for k, v in ours.state_dict().items()}
+    theirs = {k: v for k, v in ref.state_dict().items()}
+    same_keys = set(mine) == set(theirs)
+    same_shapes = same_keys and all(tuple(mine[k].shape) == tuple(theirs[k].shape) for k in mine)
+    missing, unexpected = ref.load_state_dict(mine, strict=False)
+    rot = ref.model.rotary_emb
+    d = cfg.hidden_size // cfg.num_attention_heads
+    theta = (getattr(cfg, "rope_parameters", None) or {}).get("rope_theta", 10000.0)
+    with torch.no_grad():
+        inv = 1.0 / (theta ** (torch.arange(0, d, 2, dtype=torch.float32) / d))
+        rot.inv_freq.copy_(inv)
+        if hasattr(rot, "original_inv_freq"):
+            rot.original_inv_freq.copy_(inv)
+    x = _global_batches(cfg, 1, 2, seed=4)[0]
+    with torch.no_grad():
+        a = ours(x, labels=x)["loss"].item()
+        b = ref(input_ids=x, labels=x)["loss"].item()
+    return {"same_keys": same_keys, "same_shapes": same_shapes, "missing": list(missing),
+            "unexpected": list(unexpected), "loss_ours": a, "loss_ref": b,
+            "only_ours": sorted(set(mine) - set(theirs))[:5], "only_ref": sorted(set(theirs) - set(mine))[:5]}

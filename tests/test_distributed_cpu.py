@@ -91,6 +91,17 @@ def test_zero_training_matches_reference_framework(stage):
         assert max(abs(a - b) for a, b in zip(r["ours"], r["reference"])) < 1e-4, r
 
 
+def test_model_state_dict_interchangeable_with_reference():
+    import os
+    ref_root = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref_root, "femtotron")):
+        pytest.skip("reference not installed under baseline/_ref")
+    for r in run_ranks(W.w_reference_state_dict_interchange, 2, ref_root):
+        assert r["same_keys"] and r["same_shapes"], r
+        assert not r["missing"] and not r["unexpected"], r
+        assert abs(r["loss_ours"] - r["loss_ref"]) < 1e-5, r
+
+
 def test_zero_stages_agree():
     curves = {s: run_ranks(W.w_zero, 2, s, False)[0] for s in (0, 1, 2, 3)}
     base = curves[0]
