@@ -217,3 +217,107 @@ def test_saved_tensor_log_diff_and_activation_checkpointing():
     d = diff_saved(a, c)
     assert d["only_a"] and c.saved_bytes < a.saved_bytes, (a.summary(), c.summary())
     assert "only in a:" in format_diff(d)
+
+
+def test_schedules_equal_the_reference_action_lists():
+    """The pipeline schedules are pure data: for every (P, rank, N) they must produce the same
+    action sequence (compared by compact repr, e.g. F(0), SFRB(1,0)) as the reference's
+    gpipe_schedule / one_f_one_b_schedule (skipped when the reference is not installed)."""
+    import os
+    import sys
+    import pytest
+    root = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "baseline", "_ref")
+    if not os.path.isdir(os.path.join(root, "femtotron")):
+        pytest.skip("reference not installed under baseline/_ref")
+    sys.path.insert(0, root)
+    try:
+        from femtotron.parallel.pipeline_parallel import schedule as R
+    finally:
+        sys.path.remove(root)
+    from femtotron_b200.parallel.pipeline_parallel import schedule as O
+    for P in range(1, 5):
+        for rank in range(P):
+            for N in range(1, 9):
+                mine = [repr(a) for a in O.one_f_one_b_schedule(N, P, rank)]
+                theirs = [repr(a) for a in R.one_f_one_b_schedule(N, P, rank)]
+                assert mine == theirs, (P, rank, N, mine, theirs)
+                first, last = rank == 0, rank == P - 1
+                assert [repr(a) for a in O.gpipe_schedule(N, first, last)] == \
+                    [repr(a) for a in R.gpipe_schedule(N, first, last)], (P, rank, N)
+
+
+def test_cluster_layout_equals_the_reference():
+    """compute_cluster_layout keeps the reference's flat, padded-to-dp layout (so ZeRO-3
+    shards and checkpoints line up): every field of every parameter's spec, the shard size and
+    the padding agree for assorted parameter lists and DP sizes (skipped when the reference is
+    not installed)."""
+    import os
+    import random
+    import sys
+    import pytest
+    import torch
+    root = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "baseline", "_ref")
+    if not os.path.isdir(os.path.join(root, "femtotron")):
+        pytest.skip("reference not installed under baseline/_ref")
+    sys.path.insert(0, root)
+    try:
+        from femtotron.sharding.cluster_sharding_spec import compute_cluster_layout as ref_layout
+    finally:
+        sys.path.remove(root)
+    from femtotron_b200.sharding.cluster_sharding_spec import compute_cluster_layout
+    rng = random.Random(0)
+    fields = ("global_offset", "numel", "original_shape", "original_dtype", "has_local_view",
+              "local_offset", "local_numel")
+    for trial in range(40):
+        shapes = [torch.Size([rng.randint(1, 40)] + ([rng.randint(1, 9)] if rng.random() < 0.6 else []))
+                  for _ in range(rng.randint(1, 7))]
+        numels = [s.numel() for s in shapes]
+        dtypes = [torch.float32] * len(shapes)
+        dp = rng.randint(1, 8)
+        for rank in range(dp):
+            a = compute_cluster_layout(numels, shapes, dtypes, rank, dp)
+            b = ref_layout(numels, shapes, dtypes, rank, dp)
+            assert a[1:] == tuple(b[1:]), (trial, rank, a[1:], b[1:])
+            for x, y in zip(a[0], b[0]):
+                assert all(getattr(x, f) == getattr(y, f) for f in fields), (trial, rank, x, y)
+
+
+def test_lr_schedule_and_param_groups_equal_the_reference():
+    """The LR multiplier (linear warm-up with the reference's current_step+1 shift, cosine to
+    min_lr_ratio) and the weight-decay grouping equal the reference's for the same inputs
+    (skipped when the reference is not installed)."""
+    import os
+    import sys
+    import pytest
+    import torch
+    from common_models import tiny_config
+    root = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "baseline", "_ref")
+    if not os.path.isdir(os.path.join(root, "femtotron")):
+        pytest.skip("reference not installed under baseline/_ref")
+    sys.path.insert(0, root)
+    try:
+        from femtotron.training.lr_schedule import create_lr_schedule as ref_lr
+        from femtotron.training.optimizer import get_param_groups as ref_groups
+    finally:
+        sys.path.remove(root)
+    from femtotron_b200.models import LlamaForTraining, materialize_model
+    from femtotron_b200.training import create_lr_schedule, get_param_groups
+    for warm, total, mn in ((0, 10, 0.1), (3, 20, 0.0), (10, 10, 0.5), (5, 100, 0.1)):
+        curves = []
+        for make in (create_lr_schedule, ref_lr):
+            opt = torch.optim.SGD([torch.nn.Parameter(torch.zeros(1))], lr=1.0)
+            sch = make(opt, warm, total, mn)
+            lrs = []
+            for _ in range(total + 3):
+                lrs.append(opt.param_groups[0]["lr"])
+                opt.step()
+                sch.step()
+            curves.append(lrs)
+        assert curves[0] == pytest.approx(curves[1], abs=1e-12), (warm, total, mn)
+    with torch.device("meta"):
+        m = LlamaForTraining(tiny_config())
+    materialize_model(m, "cpu", dtype=torch.float32, init_std=0.02)
+    names = {id(p): n for n, p in m.named_parameters()}
+    for a, b in zip(get_param_groups(m, 0.03), ref_groups(m, 0.03)):
+        assert a["weight_decay"] == b["weight_decay"]
+        assert [names[id(p)] for p in a["params"]] == [names[id(p)] for p in b["params"]]
