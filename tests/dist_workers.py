@@ -690,3 +690,87 @@ def w_reference_state_dict_interchange(rank, world, ref_root):
     return {"same_keys": same_keys, "same_shapes": same_shapes, "missing": list(missing),
             "unexpected": list(unexpected), "loss_ours": a, "loss_ref": b,
             "only_ours": sorted(set(mine) - set(theirs))[:5], "only_ref": sorted(set(theirs) - set(mine))[:5]}
+
+
+def _reference_mp(ref_root, cfg, sd, rctx, stage, steps, lr=5e-3):
+    """The reference's model + MixedPrecisionManager (torch AdamW) + LR schedule on CPU."""
+    from femtotron_b200.models.model_loader import shard_for_rank
+    from femtotron_b200.models.parallel_plan import get_llama_parallel_plan
+    _, rbuild = _load_reference(ref_root)
+    from femtotron.model.parallel_plan import get_llama_parallel_plan as rplan
+    from femtotron.training.train_config import TrainConfig as RTC
+    from femtotron.training.optimizer import get_param_groups as rgroups
+    from femtotron.training.mixed_precision_manager import MixedPrecisionManager as RMP
+    from femtotron.training.lr_schedule import create_lr_schedule as rlr
+    from femtotron.sharding.factory import create_sharding_strategy as rstrat
+    from femtotron.sharding.zero_config import ZeROConfig as RZ
+    from femtotron.scripts.presets import get_wrap_policy
+    from femtotron.parallel.data_parallel.gradient_synchronizer import create_grad_synchronizer as rsync
+    ref = rbuild(cfg, rctx).to_empty(device="cpu")
+    plan = get_llama_parallel_plan()
+    with torch.no_grad():
+        for name, p in ref.named_parameters():
+            p.copy_(shard_for_rank(sd[name], name, plan, rctx.tp_rank, rctx.tp_size))
+        rot = ref.model.rotary_emb
+        d = cfg.hidden_size // cfg.num_attention_heads
+        theta = (getattr(cfg, "rope_parameters", None) or {}).get("rope_theta", 10000.0)
+        inv = 1.0 / (theta ** (torch.arange(0, d, 2, dtype=torch.float32) / d))
+        rot.inv_freq.copy_(inv)
+        if hasattr(rot, "original_inv_freq"):
+            rot.original_inv_freq.copy_(inv)
+    tc = RTC(master_dtype=torch.float32, param_dtype=torch.float32, grad_clip=None,
+             train_steps=steps, log_interval=10 ** 6, checkpoint_interval=10 ** 6, warmup_steps=1,
+             min_lr_ratio=0.1, lr=lr)
+    wrap = get_wrap_policy("llama_decoder_layer") if stage == 3 else None
+    strategy = rstrat(rctx, RZ(stage=stage, wrap_policy=wrap))
+    mp = RMP(model=ref, sharding_strategy=strategy, parallel_ctx=rctx, parallel_plan=rplan(),
+             config=tc, inner_optimizer_cls=torch.optim.AdamW,
+             inner_optimizer_kwargs={"lr": lr, "betas": (0.9, 0.95), "eps": 1e-8},
+             compute_param_groups=rgroups(ref, weight_decay=0.01))
+    sched = rlr(mp.inner, warmup_steps=1, total_steps=steps, min_lr_ratio=0.1)
+    gs = rsync(mp.groups, rctx, strategy)
+    mp.strategy.prepare_for_backward(mp.groups)
+    return ref, mp, sched, gs
+
+
+def w_reference_checkpoint_resume(rank, world, ref_root, stage):
+    """A user switching frameworks mid-run: the reference trains 2 steps and its checkpoint
+    pieces (model state dict, MixedPrecisionManager state dict, scheduler state dict) are
+    loaded into this package's trainer, which continues 2 steps; the reference continues too.
+    The continued loss curves must agree."""
+    from collections import OrderedDict
+    RCtx, _ = _load_reference(ref_root)
+    cfg = tiny_config()
+    cfg.use_cache = False
+    sd = full_state(cfg)
+    steps = 4
+    batches = [b[rank * 2:(rank + 1) * 2] for b in _global_batches(cfg, steps, 2 * world, seed=17)]
+    rctx = RCtx(OrderedDict([("pp", 1), ("dp", world), ("tp", 1)]))
+    ref, mp, sched, gs = _reference_mp(ref_root, cfg, sd, rctx, stage, steps)
+
+    def ref_step(x):
+        loss = ref(input_ids=x, labels=x)["loss"]
+        loss.backward()
+        gs.sync_gradients()
+        with torch.no_grad():
+            mp.step()
+        sched.step()
+        return loss.item()
+    for x in batches[:2]:
+        ref_step(x)
+    # a checkpoint is a snapshot: state dicts hold live tensors on CPU, so round-trip them
+    # through torch.save as the reference's Trainer does
+    import io
+    buf = io.BytesIO()
+    torch.save({"model": ref.state_dict(), "optimizer": mp.state_dict(),
+                "scheduler": sched.state_dict()}, buf)
+    buf.seek(0)
+    ckpt = torch.load(buf, weights_only=False)
+    theirs = [ref_step(x) for x in batches[2:]]
+
+    tr = _build_trainer(cfg, sd, ctx_of(dp=world), stage, steps=steps, mb=2, ga=1, seed_data=1)
+    tr.model.load_state_dict(ckpt["model"], strict=False)
+    tr.mp_manager.load_state_dict(ckpt["optimizer"])
+    tr.scheduler.load_state_dict(ckpt["scheduler"])
+    ours = [tr.train_step(iter([{"input_ids": x, "labels": x}]))["loss"] for x in batches[2:]]
+    return {"ours": ours, "reference": theirs}

@@ -102,6 +102,20 @@ def test_model_state_dict_interchangeable_with_reference():
         assert abs(r["loss_ours"] - r["loss_ref"]) < 1e-5, r
 
 
+@pytest.mark.parametrize("stage", [0, 1, 2])
+def test_resume_from_a_reference_checkpoint(stage):
+    """A reference run's checkpoint pieces (model, MixedPrecisionManager and scheduler state
+    dicts) resume in this package's trainer and continue exactly like the reference.  ZeRO-3 is
+    left out: the reference does not save ZeRO-3 cluster masters, so its own runs cannot resume
+    from such a checkpoint either."""
+    import os
+    ref_root = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref_root, "femtotron")):
+        pytest.skip("reference not installed under baseline/_ref")
+    for r in run_ranks(W.w_reference_checkpoint_resume, 2, ref_root, stage, timeout=600.0):
+        assert max(abs(a - b) for a, b in zip(r["ours"], r["reference"])) < 1e-5, r
+
+
 def test_zero_stages_agree():
     curves = {s: run_ranks(W.w_zero, 2, s, False)[0] for s in (0, 1, 2, 3)}
     base = curves[0]
