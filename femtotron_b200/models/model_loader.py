@@ -31,6 +31,12 @@ def shard_for_rank(full: torch.Tensor, name: str, plan, rank: int, world: int) -
     return resolve_loader(rule, name).load(full, rank, world)
 
 
+def load_one_param(f, name: str, rule, rank: int, world_size: int) -> torch.Tensor:
+    """This rank's slice of tensor `name` from an open safetensors handle `f` (``safe_open``),
+    sliced by `rule` (column / row / vocab / replicate; None = replicate)."""
+    return resolve_loader(rule, name).load(f.get_slice(name), rank, world_size)
+
+
 class ModelLoader:
     def __init__(self, parallel_ctx):
         self.parallel_ctx = parallel_ctx
@@ -74,7 +80,7 @@ class ModelLoader:
             with safe_open(fname, framework="pt", device=str(device)) as f:
                 for key, p in items:
                     rule = plan.get_rule(_module_name(key)) if world > 1 else None
-                    t = resolve_loader(rule, key).load(f.get_slice(key), rank, world)
+                    t = load_one_param(f, key, rule, rank, world)
                     if tuple(t.shape) != tuple(p.shape):
                         raise ValueError(f"{key}: checkpoint slice {tuple(t.shape)} != parameter {tuple(p.shape)}")
                     if p.device.type == "meta":

@@ -321,3 +321,38 @@ def test_lr_schedule_and_param_groups_equal_the_reference():
     for a, b in zip(get_param_groups(m, 0.03), ref_groups(m, 0.03)):
         assert a["weight_decay"] == b["weight_decay"]
         assert [names[id(p)] for p in a["params"]] == [names[id(p)] for p in b["params"]]
+
+
+def test_reference_import_paths_and_public_names_exist():
+    """Every module of the reference package has a same-path module here
+    (femtotron.X.Y -> femtotron_b200.X.Y), and every public top-level class and function of the
+    reference module exists in it, so code written against the reference's imports resolves.
+    The reference's names are read from its source (no import); skipped without it."""
+    import ast
+    import importlib
+    import os
+    import pytest
+    root = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "baseline", "_ref")
+    pkg = os.path.join(root, "femtotron")
+    if not os.path.isdir(pkg):
+        pytest.skip("reference not installed under baseline/_ref")
+    missing = []
+    for dirpath, _, files in os.walk(pkg):
+        if f"{os.sep}test" in dirpath[len(pkg):]:
+            continue
+        for fn in files:
+            if not fn.endswith(".py"):
+                continue
+            rel = os.path.relpath(os.path.join(dirpath, fn), root)[:-3].replace(os.sep, ".")
+            rel = rel[:-len(".__init__")] if rel.endswith(".__init__") else rel
+            with open(os.path.join(dirpath, fn)) as f:
+                tree = ast.parse(f.read())
+            names = [n.name for n in tree.body if isinstance(n, (ast.FunctionDef, ast.ClassDef))
+                     and not n.name.startswith("_")]
+            try:
+                ours = importlib.import_module("femtotron_b200" + rel[len("femtotron"):])
+            except ImportError:
+                missing.append(rel)
+                continue
+            missing += [f"{rel}.{n}" for n in names if not hasattr(ours, n)]
+    assert not missing, missing
