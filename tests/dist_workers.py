@@ -774,3 +774,54 @@ def w_reference_checkpoint_resume(rank, world, ref_root, stage):
     tr.scheduler.load_state_dict(ckpt["scheduler"])
     ours = [tr.train_step(iter([{"input_ids": x, "labels": x}]))["loss"] for x in batches[2:]]
     return {"ours": ours, "reference": theirs}
+
+
+# ----------------------------------------------------------------------------- 3D parallelism
+def w_3d(rank, world, stage, steps, gb):
+    """TP=2 x PP=2 x DP=2 (1F1B, two micro-batches per step) with ZeRO `stage`: the loss curve
+    on fixed global batches must equal a single process training on the same batches."""
+    from femtotron_b200.models import build_llama_model, get_llama_parallel_plan, materialize_model
+    from femtotron_b200.parallel.data_parallel import create_grad_synchronizer
+    from femtotron_b200.parallel.pipeline_parallel import (PipelineComm, PipelineRunner, PipelineStage,
+                                                           partition_layers)
+    from femtotron_b200.parallel.pipeline_parallel.pipeline_config import PipelineConfig
+    from femtotron_b200.sharding import ZeROConfig, create_sharding_strategy, llama_wrap_policy
+    from femtotron_b200.training import (FusedAdamW, MixedPrecisionManager, TrainConfig, Trainer,
+                                         create_lr_schedule, get_param_groups)
+    cfg = tiny_config(num_hidden_layers=4, num_key_value_heads=2)
+    sd = full_state(cfg)
+    ctx = ctx_of(pp=2, dp=2, tp=2)
+    nmb, seq = 2, 32
+    per_rank = gb // ctx.dp_size
+    rng = partition_layers(cfg.num_hidden_layers, ctx.pp_size)[ctx.pp_rank]
+    m = build_llama_model(cfg, ctx, use_pp_aware=True, layer_range=rng)
+    materialize_model(m, "cpu", dtype=torch.float32, init_std=None)
+    load_sharded(m, sd, ctx)
+    tc = TrainConfig(train_steps=steps, grad_accum_steps=1, master_dtype=torch.float32,
+                     param_dtype=torch.float32, log_interval=10 ** 6, checkpoint_interval=10 ** 6,
+                     warmup_steps=1, min_lr_ratio=0.1, pipeline_config=PipelineConfig(nmb, "1f1b"))
+    st = create_sharding_strategy(ctx, ZeROConfig(stage=stage, wrap_policy=llama_wrap_policy))
+    mp = MixedPrecisionManager(m, ctx, get_llama_parallel_plan(), tc, FusedAdamW,
+                               dict(lr=5e-3, betas=(0.9, 0.95), eps=1e-8), get_param_groups(m, 0.01),
+                               sharding_strategy=st)
+    sch = create_lr_schedule(mp.inner, 1, steps)
+    stage_ = PipelineStage(m, ctx, loss_scale=1.0 / nmb)
+    comm = PipelineComm(ctx, seq, cfg.hidden_size, torch.float32, device=torch.device("cpu"))
+    runner = PipelineRunner(stage_, comm, schedule_name="1f1b", num_microbatches=nmb,
+                            recv_shape=(per_rank // nmb, seq, cfg.hidden_size), recv_dtype=torch.float32)
+    tr = Trainer(m, mp, sch, None, create_grad_synchronizer(mp.groups, ctx, st), ctx, tc, pp_runner=runner)
+    batches = _global_batches(cfg, steps, gb, seq=seq, seed=29)
+    r = ctx.dp_rank
+    losses = []
+    for b in batches:
+        x = b[r * per_rank:(r + 1) * per_rank]
+        losses.append(tr.train_step(iter([{"input_ids": x, "labels": x}]))["loss"])
+    t = torch.tensor(losses, dtype=torch.float64)
+    dist.all_reduce(t)
+    return (t / world).tolist()
+
+
+def w_3d_single(rank, world, steps, gb):
+    cfg = tiny_config(num_hidden_layers=4, num_key_value_heads=2)
+    sd = full_state(cfg)
+    return _run_split(cfg, sd, ctx_of(dp=1), 0, steps=steps, mb=gb, ga=1, seed=29)

@@ -116,6 +116,16 @@ def test_resume_from_a_reference_checkpoint(stage):
         assert max(abs(a - b) for a, b in zip(r["ours"], r["reference"])) < 1e-5, r
 
 
+@pytest.mark.parametrize("stage", [1, 3])
+def test_3d_tp2_pp2_dp2_matches_single_process(stage):
+    """BASELINE configuration 4's composition (TP=2 x PP=2 x DP=2, 1F1B, ZeRO) at tiny scale on
+    eight CPU ranks, against one process on the same global batches."""
+    ref = run_ranks(W.w_3d_single, 1, 3, 8)[0]
+    res = run_ranks(W.w_3d, 8, stage, 3, 8, timeout=600.0)
+    for r in res:
+        assert max(abs(a - b) for a, b in zip(r, ref)) < 1e-4, (r, ref)
+
+
 def test_zero_stages_agree():
     curves = {s: run_ranks(W.w_zero, 2, s, False)[0] for s in (0, 1, 2, 3)}
     base = curves[0]
