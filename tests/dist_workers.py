@@ -388,13 +388,13 @@ def _global_batches(cfg, steps, gb, seq=32, seed=21):
     return [torch.randint(0, cfg.vocab_size, (gb, seq), generator=g) for _ in range(steps)]
 
 
-def _run_split(cfg, sd, ctx, stage, steps, mb, ga, seed=21):
+def _run_split(cfg, sd, ctx, stage, steps, mb, ga, seed=21, ac=False):
     """Train `steps` optimizer steps where global step s consumes the fixed global batch G_s
     (dp x ga x mb rows): DP rank r, micro-batch k takes rows [(r*ga + k)*mb, ... + mb).
     Returns the loss curve averaged over all ranks (= the global-batch mean)."""
     gb = ctx.dp_size * ga * mb
     batches = _global_batches(cfg, steps, gb, seed=seed)
-    tr = _build_trainer(cfg, sd, ctx, stage, steps=steps, mb=mb, ga=ga, seed_data=1)
+    tr = _build_trainer(cfg, sd, ctx, stage, steps=steps, mb=mb, ga=ga, seed_data=1, ac=ac)
     r = ctx.dp_rank
     losses = []
     for s in range(steps):
@@ -408,11 +408,12 @@ def _run_split(cfg, sd, ctx, stage, steps, mb, ga, seed=21):
     return (t / dist.get_world_size()).tolist()
 
 
-def w_dp_tp_split(rank, world, dp, tp, stage):
-    """Reference test_dp_training: the same global batches under every legal (DP, TP) split."""
+def w_dp_tp_split(rank, world, dp, tp, stage, ac=False):
+    """Reference test_dp_training: the same global batches under every legal (DP, TP) split
+    (optionally with ZeRO and activation checkpointing)."""
     cfg = tiny_config(num_key_value_heads=4)
     sd = full_state(cfg)
-    return _run_split(cfg, sd, ctx_of(dp=dp, tp=tp), stage, steps=3, mb=8 // dp, ga=1)
+    return _run_split(cfg, sd, ctx_of(dp=dp, tp=tp), stage, steps=3, mb=8 // dp, ga=1, ac=ac)
 
 
 def w_grad_accum(rank, world, mb, ga):

@@ -48,6 +48,14 @@ def test_dp_tp_splits_agree():
     assert base[-1] < base[0]
 
 
+def test_tp2_zero3_dp2_with_activation_checkpointing_agrees():
+    """BASELINE configuration 5's composition (TP x ZeRO-3 DP with full activation
+    checkpointing) at tiny scale on four ranks, against plain DP=4."""
+    base = run_ranks(W.w_dp_tp_split, 4, 4, 1, 0)[0]
+    c = run_ranks(W.w_dp_tp_split, 4, 2, 2, 3, True)[0]
+    assert max(abs(a - b) for a, b in zip(c, base)) < 1e-4, (c, base)
+
+
 def test_gradient_accumulation_splits_agree():
     curves = {(mb, ga): run_ranks(W.w_grad_accum, 2, mb, ga)[0] for mb, ga in ((4, 1), (2, 2), (1, 4))}
     base = curves[(4, 1)]
