@@ -101,4 +101,8 @@ class PipelineComm:
                 r.wait()  # stream-ordered: makes the comm stream wait, not the host
         for t in tensors:
             t.record_stream(self._stream)
-        cur.wait_stream(self._stream)
+        # Only a receive has a consumer on the compute stream; a pure send lets the compute
+        # stream run on (the caching allocator keeps the sent tensor alive through
+        # record_stream, and sent activations / gradients are not modified in place).
+        if any(fn is dist.irecv for fn, _, _ in specs):
+            cur.wait_stream(self._stream)
