@@ -826,3 +826,45 @@ def w_3d_single(rank, world, steps, gb):
     cfg = tiny_config(num_hidden_layers=4, num_key_value_heads=2)
     sd = full_state(cfg)
     return _run_split(cfg, sd, ctx_of(dp=1), 0, steps=steps, mb=gb, ga=1, seed=29)
+
+
+# ----------------------------------------------------------------------------- TP comm ops
+def w_tp_comm_ops(rank, world):
+    """The six TP / SP autograd communication ops against their single-process meaning, on
+    `world` ranks: forward values and input gradients of y = op(x) with loss sum(y * w)."""
+    from femtotron_b200.parallel.tensor_parallel import comm_ops as C
+    ctx = ctx_of(tp=world)
+    g = ctx.tp_group
+    torch.manual_seed(0)
+    full = torch.randn(4 * world, 6 * world)          # the same on every rank
+    wfull = torch.randn(4 * world, 6 * world)
+    rows, cols = full.shape[0] // world, full.shape[1] // world
+    res = {}
+
+    def run(op, x, w):
+        x = x.clone().requires_grad_(True)
+        y = op(x)
+        (y * w).sum().backward()
+        return y.detach(), x.grad
+    # scatter along the last dim: y = own column block; dx = all-gathered (zero-free) w blocks
+    y, dx = run(lambda x: C.scatter_to_tp(x, g, -1), full, wfull[:, rank * cols:(rank + 1) * cols])
+    res["scatter_fwd"] = torch.equal(y, full[:, rank * cols:(rank + 1) * cols])
+    wblocks = [wfull[:, r * cols:(r + 1) * cols] for r in range(world)]
+    res["scatter_bwd"] = torch.allclose(dx, torch.cat(wblocks, 1))
+    # gather along the last dim: y = full; dx = own block of w
+    y, dx = run(lambda x: C.gather_from_tp(x, g, -1), full[:, rank * cols:(rank + 1) * cols], wfull)
+    res["gather_fwd"] = torch.equal(y, full)
+    res["gather_bwd"] = torch.allclose(dx, wfull[:, rank * cols:(rank + 1) * cols])
+    # copy (identity forward, all-reduce backward) and reduce (all-reduce forward, identity backward)
+    y, dx = run(lambda x: C.copy_to_tp(x, g), full, wfull * (rank + 1))
+    res["copy"] = torch.equal(y, full) and torch.allclose(dx, wfull * sum(range(1, world + 1)))
+    y, dx = run(lambda x: C.reduce_from_tp(x, g), full * (rank + 1), wfull)
+    res["reduce"] = torch.allclose(y, full * sum(range(1, world + 1))) and torch.allclose(dx, wfull)
+    # sequence parallel: gather rows (backward reduce-scatters), reduce-scatter rows (backward gathers)
+    y, dx = run(lambda x: C.gather_from_sp(x, g), full[rank * rows:(rank + 1) * rows], wfull * (rank + 1))
+    res["sp_gather"] = torch.equal(y, full) and torch.allclose(
+        dx, (wfull * sum(range(1, world + 1)))[rank * rows:(rank + 1) * rows])
+    y, dx = run(lambda x: C.reduce_scatter_to_sp(x, g), full * (rank + 1), wfull[rank * rows:(rank + 1) * rows])
+    res["sp_reduce_scatter"] = torch.allclose(y, (full * sum(range(1, world + 1)))[rank * rows:(rank + 1) * rows]) \
+        and torch.allclose(dx, wfull)
+    return res

@@ -24,6 +24,14 @@ def test_tp_layers_match_full(sp):
         assert all(r.values()), r
 
 
+@pytest.mark.parametrize("world", [2, 4])
+def test_tp_comm_ops_forward_and_backward(world):
+    """Copy/Reduce/Gather/Scatter to the TP region and the sequence-parallel gather /
+    reduce-scatter (the reference's scatter is broken: wrong chunk size, wrong backward arity)."""
+    for r in run_ranks(W.w_tp_comm_ops, world):
+        assert all(r.values()), r
+
+
 @pytest.mark.parametrize("sp", [False, True])
 def test_tp_model_matches_single_process(sp):
     for r in run_ranks(W.w_tp_model, 2, sp):
