@@ -868,3 +868,53 @@ def w_tp_comm_ops(rank, world):
     res["sp_reduce_scatter"] = torch.allclose(y, (full * sum(range(1, world + 1)))[rank * rows:(rank + 1) * rows]) \
         and torch.allclose(dx, wfull)
     return res
+
+
+# ----------------------------------------------------------------------------- ParamGroupCluster
+def w_param_group_cluster(rank, world):
+    """Reference test_param_group_cluster semantics on gloo ranks: a cluster takes over its
+    parameter groups (compute data becomes a placeholder), holds this rank's slice of the
+    padded flat buffer, unshard restores every parameter exactly, reshard drops it again, and a
+    reduce-scatter of per-rank gradients yields this rank's slice of their mean."""
+    from femtotron_b200.models import LlamaForTraining, materialize_model
+    from femtotron_b200.models.parallel_plan import get_llama_parallel_plan
+    from femtotron_b200.sharding.param_group_cluster import ParamGroupCluster
+    from femtotron_b200.training.param_group import ParamGroup
+    cfg = tiny_config(num_hidden_layers=1)
+    sd = full_state(cfg)
+    ctx = ctx_of(dp=world)
+    with torch.device("meta"):
+        m = LlamaForTraining(cfg)
+    materialize_model(m, "cpu", dtype=torch.float32, init_std=None)
+    m.load_state_dict(sd)
+    layer = m.model.layers["0"] if hasattr(m.model.layers, "keys") else m.model.layers[0]
+    names = {p: n for n, p in m.named_parameters()}
+    pgs = [ParamGroup(names[p], p, None, {}, ctx, get_llama_parallel_plan()) for p in layer.parameters()]
+    originals = {pg.name: pg.compute.detach().clone() for pg in pgs}
+    total = sum(t.numel() for t in originals.values())
+    c = ParamGroupCluster("layer0", layer, pgs, ctx.dp_group, torch.float32)
+    out = {}
+    out["claimed"] = all(pg.cluster is c for pg in pgs)
+    out["placeholders"] = all(pg.compute.numel() == 0 for pg in pgs)
+    out["shard_size"] = c.shard_size == -(-total // world) and c.padded_size == c.shard_size * world
+    flat = torch.cat([originals[pg.name].reshape(-1) for pg in pgs])
+    flat = torch.cat([flat, flat.new_zeros(c.padded_size - total)])
+    out["shard_content"] = torch.equal(c.flat_param_shard, flat[rank * c.shard_size:(rank + 1) * c.shard_size])
+    c.unshard()
+    out["unshard_restores"] = all(torch.equal(pg.compute.detach(), originals[pg.name]) for pg in pgs)
+    c.reshard()
+    out["reshard_drops"] = all(pg.compute.numel() == 0 for pg in pgs)
+    # reduce-scatter (AVG) of per-rank gradients
+    c.unshard()
+    c.prepare_grad_buffer()
+    for pg in pgs:
+        pg.compute.main_grad.copy_(torch.full_like(pg.compute.main_grad, float(rank + 1)))
+    c.reduce_scatter_grads()
+    c.reshard()
+    mean = sum(range(1, world + 1)) / world
+    want = torch.full((c.shard_size,), mean)
+    lo = rank * c.shard_size
+    pad_from = max(0, min(c.shard_size, total - lo))   # padding reduces to zero
+    want[pad_from:] = 0.0
+    out["reduce_scatter_mean"] = torch.allclose(c.flat_grad_shard, want)
+    return out

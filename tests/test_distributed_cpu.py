@@ -142,6 +142,12 @@ def test_3d_tp2_pp2_dp2_matches_single_process(stage):
         assert max(abs(a - b) for a, b in zip(r, ref)) < 1e-4, (r, ref)
 
 
+@pytest.mark.parametrize("world", [2, 3])
+def test_param_group_cluster_semantics(world):
+    for r in run_ranks(W.w_param_group_cluster, world):
+        assert all(r.values()), r
+
+
 def test_zero_stages_agree():
     curves = {s: run_ranks(W.w_zero, 2, s, False)[0] for s in (0, 1, 2, 3)}
     base = curves[0]
