@@ -918,3 +918,38 @@ def w_param_group_cluster(rank, world):
     want[pad_from:] = 0.0
     out["reduce_scatter_mean"] = torch.allclose(c.flat_grad_shard, want)
     return out
+
+
+# ----------------------------------------------------------------------------- PipelineComm
+def w_pipeline_comm(rank, world):
+    """Reference test_pipeline_comm on two pipeline ranks: forward / backward round trips, the
+    combined send+recv operations of 1F1B's steady state (both sides submit at once without
+    deadlocking), edge-stage no-ops, buffer validation and dtypes."""
+    from femtotron_b200.parallel.pipeline_parallel import PipelineComm
+    ctx = ctx_of(pp=world)
+    out = {}
+    for dtype in (torch.float32, torch.bfloat16):
+        comm = PipelineComm(ctx, 8, 16, dtype, device=torch.device("cpu"))
+        act = torch.full((8, 16), 1.0 + rank, dtype=dtype)
+        if rank == 0:
+            comm.send_forward(act)
+            g = comm.recv_backward()
+            out[f"roundtrip_{dtype}"] = torch.equal(g, torch.full((8, 16), 10.0, dtype=dtype))
+            out[f"first_recv_forward_none_{dtype}"] = comm.recv_forward() is None
+            # steady state: send activation i+1, receive gradient i, in one submission
+            g2 = comm.send_forward_recv_backward(act * 2)
+            out[f"sfrb_{dtype}"] = torch.equal(g2, torch.full((8, 16), 20.0, dtype=dtype))
+        else:
+            x = comm.recv_forward()
+            out[f"roundtrip_{dtype}"] = torch.equal(x, torch.full((8, 16), 1.0, dtype=dtype))
+            comm.send_backward(torch.full((8, 16), 10.0, dtype=dtype))
+            out[f"last_recv_backward_none_{dtype}"] = comm.recv_backward() is None
+            x2 = comm.send_backward_recv_forward(torch.full((8, 16), 20.0, dtype=dtype))
+            out[f"sbrf_{dtype}"] = torch.equal(x2, torch.full((8, 16), 2.0, dtype=dtype))
+    comm = PipelineComm(ctx, 8, 16, torch.float32, device=torch.device("cpu"))
+    try:
+        comm._buf(torch.empty(8, 16, dtype=torch.bfloat16))
+        out["bad_dtype_refused"] = False
+    except ValueError:
+        out["bad_dtype_refused"] = True
+    return out

@@ -78,6 +78,11 @@ def test_grad_norm_matches_torch_clip_grad_norm(tp):
             assert abs(r[f"zero{stage}"] - r["torch"]) < 1e-4 * r["torch"], (stage, r)
 
 
+def test_pipeline_comm_round_trips_and_combined_ops():
+    for r in run_ranks(W.w_pipeline_comm, 2, timeout=120.0, pg_timeout=30.0):
+        assert all(r.values()), r
+
+
 def test_pipeline_stage_call_order_and_state():
     r = run_ranks(W.w_stage_errors, 1)[0]
     assert all(r.values()), r
