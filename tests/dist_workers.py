@@ -953,3 +953,39 @@ def w_pipeline_comm(rank, world):
     except ValueError:
         out["bad_dtype_refused"] = True
     return out
+
+
+# ----------------------------------------------------------------------------- memory ordering
+def w_state_bytes(rank, world):
+    """Reference test_zero1_2_3 memory ordering, as persistent state per rank after one step:
+    compute parameters + fp32 masters + AdamW moments (+ ZeRO-3 cluster shards).  ZeRO-1 keeps
+    1/dp of ZeRO-0's masters and moments; ZeRO-3 also shards the compute parameters."""
+    cfg = tiny_config()
+    sd = full_state(cfg)
+    x = _global_batches(cfg, 1, 2 * world, seed=3)[0][rank * 2:(rank + 1) * 2]
+    out = {}
+    for stage in (0, 1, 2, 3):
+        tr = _build_trainer(cfg, sd, ctx_of(dp=world), stage, steps=1, mb=2, ga=1, seed_data=1)
+        tr.train_step(iter([{"input_ids": x, "labels": x}]))
+        mp = tr.mp_manager
+        tr.mp_manager.strategy.force_reshard_all() if stage == 3 else None
+        seen, total = set(), 0
+
+        def add(t):
+            nonlocal total
+            if t is not None and t.numel() and t.data_ptr() not in seen:
+                seen.add(t.data_ptr())
+                total += t.numel() * t.element_size()
+        for p in tr.model.parameters():
+            add(p.data)
+        for g in mp.groups:
+            add(g.master)
+        for c in mp.clusters:
+            add(c.flat_param_shard)
+            add(c.master)
+        for st in mp.inner.state.values():
+            for v in st.values():
+                if torch.is_tensor(v) and v.dim() > 0:
+                    add(v)
+        out[stage] = total
+    return out

@@ -153,6 +153,12 @@ def test_param_group_cluster_semantics(world):
         assert all(r.values()), r
 
 
+def test_zero_state_memory_ordering():
+    for r in run_ranks(W.w_state_bytes, 2):
+        assert r[1] < r[0] and r[2] <= r[1] and r[3] < r[1], r
+        assert r[1] < 0.75 * r[0], r   # masters + moments halve at dp=2; compute params stay full
+
+
 def test_zero_stages_agree():
     curves = {s: run_ranks(W.w_zero, 2, s, False)[0] for s in (0, 1, 2, 3)}
     base = curves[0]
