@@ -519,7 +519,7 @@ def _load_reference(ref_root):
 def w_reference_parity(rank, world, ref_root, steps):
     """BASELINE configuration 1 against the reference's own modules on the same gloo ranks:
     tiny LLaMA (4 layers, hidden 256, 8/4 heads, FFN 688, vocab 2048), TP=2, fp32, seq 128,
-    micro-batch 4, uniform token ids from seed 0, identical initial weights.  Both sides run
+    micro-batch 4, uniform token ids from seed 0, identical initial weights, `steps` steps.  Both sides run
     forward + backward of their own model and an identical AdamW update of the full
     parameters, so the loss curves must agree."""
     from collections import OrderedDict

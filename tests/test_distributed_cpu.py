@@ -89,14 +89,14 @@ def test_pipeline_stage_call_order_and_state():
 
 
 def test_tiny_tp2_matches_reference_modules():
-    """BASELINE configuration 1 with the reference's own code as the oracle (skipped when the
-    reference is not installed under baseline/_ref)."""
+    """BASELINE configuration 1 with the reference's own code as the oracle, over 100 AdamW
+    steps (skipped when the reference is not installed under baseline/_ref)."""
     import os
     ref_root = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "baseline", "_ref")
     if not os.path.isdir(os.path.join(ref_root, "femtotron")):
         pytest.skip("reference not installed under baseline/_ref")
-    for r in run_ranks(W.w_reference_parity, 2, ref_root, 10, timeout=600.0):
-        assert len(r["ours"]) == 10
+    for r in run_ranks(W.w_reference_parity, 2, ref_root, 100, timeout=900.0):
+        assert len(r["ours"]) == 100
         assert max(abs(a - b) for a, b in zip(r["ours"], r["reference"])) < 1e-4, r
 
 
