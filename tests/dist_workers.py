@@ -126,7 +126,7 @@ def _inject_delays(model, seed, max_s=0.02):
 
 
 def _build_trainer(cfg, sd, ctx, stage, steps, mb, ga, seed_data, lr=5e-3, clip=None, ckpt=None,
-                   ac=False, delay_seed=None, check_finite=False):
+                   ac=False, delay_seed=None, check_finite=False, dtype=torch.float32):
     from femtotron_b200.data import DistributedDataLoader, SyntheticTokens, simple_pretrain_collator
     from femtotron_b200.models import build_llama_model, get_llama_parallel_plan, materialize_model
     from femtotron_b200.parallel.data_parallel import create_grad_synchronizer
@@ -137,12 +137,12 @@ def _build_trainer(cfg, sd, ctx, stage, steps, mb, ga, seed_data, lr=5e-3, clip=
     from femtotron_b200.training.ckpt_policy import by_class
     from femtotron_b200.models.layers import LlamaDecoderLayer
     m = build_llama_model(cfg, ctx)
-    materialize_model(m, "cpu", dtype=torch.float32, init_std=None)
+    materialize_model(m, "cpu", dtype=dtype, init_std=None)
     load_sharded(m, sd, ctx)
     if delay_seed is not None:
         _inject_delays(m, delay_seed)
     tc = TrainConfig(train_steps=steps, grad_accum_steps=ga, master_dtype=torch.float32,
-                     param_dtype=torch.float32, log_interval=10 ** 6,
+                     param_dtype=dtype, log_interval=10 ** 6,
                      checkpoint_interval=ckpt[1] if ckpt else 10 ** 6,
                      checkpoint_dir=ckpt[0] if ckpt else "ckpt", warmup_steps=1, min_lr_ratio=0.1)
     st = create_sharding_strategy(ctx, ZeROConfig(stage=stage, wrap_policy=llama_wrap_policy))
@@ -693,7 +693,7 @@ def w_reference_state_dict_interchange(rank, world, ref_root):
             "only_ours": sorted(set(mine) - set(theirs))[:5], "only_ref": sorted(set(theirs) - set(mine))[:5]}
 
 
-def _reference_mp(ref_root, cfg, sd, rctx, stage, steps, lr=5e-3):
+def _reference_mp(ref_root, cfg, sd, rctx, stage, steps, lr=5e-3, dtype=torch.float32):
     """The reference's model + MixedPrecisionManager (torch AdamW) + LR schedule on CPU."""
     from femtotron_b200.models.model_loader import shard_for_rank
     from femtotron_b200.models.parallel_plan import get_llama_parallel_plan
@@ -719,7 +719,10 @@ def _reference_mp(ref_root, cfg, sd, rctx, stage, steps, lr=5e-3):
         rot.inv_freq.copy_(inv)
         if hasattr(rot, "original_inv_freq"):
             rot.original_inv_freq.copy_(inv)
-    tc = RTC(master_dtype=torch.float32, param_dtype=torch.float32, grad_clip=None,
+    if dtype != torch.float32:
+        ref = ref.to(dtype)   # the reference's train.py casts the model (model.bfloat16())
+        rot.inv_freq.data = rot.inv_freq.float()
+    tc = RTC(master_dtype=torch.float32, param_dtype=dtype, grad_clip=None,
              train_steps=steps, log_interval=10 ** 6, checkpoint_interval=10 ** 6, warmup_steps=1,
              min_lr_ratio=0.1, lr=lr)
     wrap = get_wrap_policy("llama_decoder_layer") if stage == 3 else None
@@ -989,3 +992,30 @@ def w_state_bytes(rank, world):
                     add(v)
         out[stage] = total
     return out
+
+
+def w_reference_bf16_parity(rank, world, ref_root, stage, steps):
+    """bf16 compute with fp32 master weights through the reference's MixedPrecisionManager and
+    through this package's, same weights and per-rank batches: loss curves agree to bf16
+    tolerance (the two compute the same math with different bf16 kernels and roundings)."""
+    from collections import OrderedDict
+    RCtx, _ = _load_reference(ref_root)
+    cfg = tiny_config()
+    cfg.use_cache = False
+    sd = full_state(cfg)
+    batches = [b[rank * 2:(rank + 1) * 2] for b in _global_batches(cfg, steps, 2 * world, seed=31)]
+    tr = _build_trainer(cfg, sd, ctx_of(dp=world), stage, steps=steps, mb=2, ga=1, seed_data=1,
+                        lr=1e-3, dtype=torch.bfloat16)
+    ours = [tr.train_step(iter([{"input_ids": x, "labels": x}]))["loss"] for x in batches]
+    rctx = RCtx(OrderedDict([("pp", 1), ("dp", world), ("tp", 1)]))
+    ref, mp, sched, gs = _reference_mp(ref_root, cfg, sd, rctx, stage, steps, lr=1e-3, dtype=torch.bfloat16)
+    theirs = []
+    for x in batches:
+        loss = ref(input_ids=x, labels=x)["loss"]
+        loss.backward()
+        gs.sync_gradients()
+        with torch.no_grad():
+            mp.step()
+        sched.step()
+        theirs.append(loss.item())
+    return {"ours": ours, "reference": theirs}

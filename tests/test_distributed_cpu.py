@@ -159,6 +159,18 @@ def test_zero_state_memory_ordering():
         assert r[1] < 0.75 * r[0], r   # masters + moments halve at dp=2; compute params stay full
 
 
+@pytest.mark.parametrize("stage", [0, 3])
+def test_bf16_mixed_precision_matches_reference_framework(stage):
+    """bf16 compute + fp32 masters through the reference's MixedPrecisionManager and this
+    package's: 30 steps on DP=2 agree to bf16 tolerance (observed max 1.3e-3 on losses ~5.6)."""
+    import os
+    ref_root = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref_root, "femtotron")):
+        pytest.skip("reference not installed under baseline/_ref")
+    for r in run_ranks(W.w_reference_bf16_parity, 2, ref_root, stage, 30, timeout=900.0):
+        assert max(abs(a - b) for a, b in zip(r["ours"], r["reference"])) < 1e-2, r
+
+
 def test_zero_stages_agree():
     curves = {s: run_ranks(W.w_zero, 2, s, False)[0] for s in (0, 1, 2, 3)}
     base = curves[0]
