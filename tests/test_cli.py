@@ -43,3 +43,19 @@ def test_cli_pipeline_1f1b(tmp_path):
                 "--seq_len", "32", "--micro_batch_size", "2", "--train_steps", "3", "--zero_stage", "1"], tmp_path)
     assert out.returncode == 0, out.stdout[-2000:] + out.stderr[-3000:]
     assert "step      3/3" in out.stdout
+
+
+def test_cli_trains_on_a_local_corpus(tmp_path):
+    """The non-synthetic data path end to end without network: a local .jsonl corpus, the
+    byte tokenizer, rank-0 preprocessing into data_dir, then TP=2 training on the packed rows."""
+    import json
+    corpus = tmp_path / "corpus.jsonl"
+    corpus.write_text("\n".join(json.dumps({"text": f"document {i}: the quick brown fox jumps over the lazy dog"})
+                                for i in range(60)) + "\n")
+    cfg = os.path.join(ROOT, "configs", "tiny_llama_debug.yaml")
+    out = _run(["--config", cfg, "--num_hidden_layers", "2", "--seq_len", "64", "--micro_batch_size", "2",
+                "--train_steps", "3", "--synthetic_data", "false", "--dataset", str(corpus),
+                "--tokenizer", "bytes", "--data_dir", str(tmp_path / "data"), "--num_samples", "60"], tmp_path)
+    assert out.returncode == 0, out.stdout[-2000:] + out.stderr[-3000:]
+    assert "step      3/3" in out.stdout
+    assert any(f.endswith("_seq64.pt") for f in os.listdir(tmp_path / "data"))

@@ -356,3 +356,26 @@ def test_reference_import_paths_and_public_names_exist():
                 continue
             missing += [f"{rel}.{n}" for n in names if not hasattr(ours, n)]
     assert not missing, missing
+
+
+def test_preprocess_local_jsonl_with_byte_tokenizer(tmp_path):
+    """Offline preprocessing: a local .jsonl corpus, the byte tokenizer (UTF-8 bytes, EOS 256),
+    documents packed into full rows each followed by EOS; PackedDataset reads the result."""
+    import json
+    import torch
+    from femtotron_b200.data import PackedDataset
+    from femtotron_b200.data.preprocess import BYTES_EOS, pack_tokens, preprocess
+    docs = ["hello world", "packed rows of tokens", "é ✓"]
+    src = tmp_path / "corpus.jsonl"
+    src.write_text("\n".join(json.dumps({"text": d}) for d in docs) + "\n")
+    out = tmp_path / "packed" / "data.pt"
+    data = preprocess(str(src), "bytes", str(out), seq_len=8)
+    stream = []
+    for d in docs:
+        stream += list(d.encode("utf-8")) + [BYTES_EOS]
+    n = len(stream) // 8
+    assert data.shape == (n, 8) and data.dtype == torch.int32
+    assert data.reshape(-1).tolist() == stream[:n * 8]
+    ds = PackedDataset(str(out))
+    assert len(ds) == n and ds.seq_len == 8
+    assert pack_tokens([[1, 2], [3]], eos=0, seq_len=3).tolist() == [[1, 2, 0]]
