@@ -73,11 +73,19 @@ DEFAULTS = dict(tp=1, pp=1, zero_stage=0, zero_wrap_policy="llama_decoder_layer"
 
 
 def load_config(args) -> dict:
+    """DEFAULTS <- YAML <- command line.  ``cfg["_explicit"]`` names the keys the user set
+    (YAML or command line), as opposed to defaults."""
     cfg = dict(DEFAULTS)
+    explicit: set[str] = set()
     if args.config:
         with open(args.config) as f:
-            cfg.update({k: v for k, v in (yaml.safe_load(f) or {}).items()})
-    cfg.update({k: v for k, v in vars(args).items() if v is not None and k != "config"})
+            y = {k: v for k, v in (yaml.safe_load(f) or {}).items()}
+        cfg.update(y)
+        explicit |= set(y)
+    cli = {k: v for k, v in vars(args).items() if v is not None and k != "config"}
+    cfg.update(cli)
+    explicit |= set(cli)
+    cfg["_explicit"] = explicit
     return cfg
 
 
@@ -85,7 +93,8 @@ def model_config_from(cfg: dict):
     from transformers import AutoConfig, LlamaConfig
     if cfg.get("model_name"):
         mc = AutoConfig.from_pretrained(cfg["model_name"])
-        if cfg.get("num_hidden_layers"):
+        # a pretrained config keeps its own depth unless the user asked for another one
+        if "num_hidden_layers" in cfg.get("_explicit", ()):
             mc.num_hidden_layers = cfg["num_hidden_layers"]
         return mc
     return LlamaConfig(hidden_size=cfg["hidden_size"], intermediate_size=cfg["intermediate_size"],

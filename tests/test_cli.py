@@ -59,3 +59,20 @@ def test_cli_trains_on_a_local_corpus(tmp_path):
     assert out.returncode == 0, out.stdout[-2000:] + out.stderr[-3000:]
     assert "step      3/3" in out.stdout
     assert any(f.endswith("_seq64.pt") for f in os.listdir(tmp_path / "data"))
+
+
+def test_cli_starts_from_a_local_hf_checkpoint(tmp_path):
+    """--model_name pointing at a local Hugging Face directory (config.json + safetensors):
+    the config comes from it and every TP rank loads its weight slices with ModelLoader."""
+    import torch
+    from transformers import LlamaConfig, LlamaForCausalLM
+    hf_dir = tmp_path / "hf"
+    cfg = LlamaConfig(hidden_size=64, intermediate_size=160, num_attention_heads=4, num_key_value_heads=2,
+                      num_hidden_layers=2, vocab_size=512, max_position_embeddings=256)
+    torch.manual_seed(0)
+    LlamaForCausalLM(cfg).save_pretrained(str(hf_dir), safe_serialization=True)
+    out = _run(["--model_name", str(hf_dir), "--tp", "2", "--seq_len", "32", "--micro_batch_size", "2",
+                "--train_steps", "2", "--warmup_steps", "1", "--log_interval", "1", "--synthetic_data", "true"],
+               tmp_path)
+    assert out.returncode == 0, out.stdout[-2000:] + out.stderr[-3000:]
+    assert "step      2/2" in out.stdout
