@@ -76,3 +76,14 @@ def test_cli_starts_from_a_local_hf_checkpoint(tmp_path):
                tmp_path)
     assert out.returncode == 0, out.stdout[-2000:] + out.stderr[-3000:]
     assert "step      2/2" in out.stdout
+
+
+def test_cli_sequence_parallel_with_clipping_and_accumulation(tmp_path):
+    """TP=2 with sequence parallelism, gradient clipping and gradient accumulation through the
+    command line (the reference's script ignores grad_accum_steps and never clips)."""
+    cfg = os.path.join(ROOT, "configs", "tiny_llama_debug.yaml")
+    out = _run(["--config", cfg, "--tp", "2", "--sequence_parallel", "true", "--num_hidden_layers", "2",
+                "--seq_len", "64", "--micro_batch_size", "2", "--grad_accum_steps", "2", "--grad_clip", "1.0",
+                "--train_steps", "3", "--zero_stage", "1"], tmp_path)
+    assert out.returncode == 0, out.stdout[-2000:] + out.stderr[-3000:]
+    assert "step      3/3" in out.stdout and "gnorm" in out.stdout
