@@ -87,3 +87,32 @@ def test_cli_sequence_parallel_with_clipping_and_accumulation(tmp_path):
                 "--train_steps", "3", "--zero_stage", "1"], tmp_path)
     assert out.returncode == 0, out.stdout[-2000:] + out.stderr[-3000:]
     assert "step      3/3" in out.stdout and "gnorm" in out.stdout
+
+
+def _losses(stdout: str) -> dict:
+    out = {}
+    for line in stdout.splitlines():
+        if line.startswith("step") and "| loss" in line:
+            step = int(line.split("/")[0].split()[-1])
+            out[step] = float(line.split("| loss")[1].split("|")[0])
+    return out
+
+
+def test_cli_pipeline_checkpoint_resume(tmp_path):
+    """PP=2 (1F1B) checkpoints carry a _pp<p> suffix per stage; resuming from step 2 reproduces
+    the uninterrupted run's losses for steps 3-4."""
+    cfg = os.path.join(ROOT, "configs", "tiny_llama_debug.yaml")
+    common = ["--config", cfg, "--tp", "1", "--pp", "2", "--num_microbatches", "2", "--num_hidden_layers", "2",
+              "--seq_len", "32", "--micro_batch_size", "2", "--train_steps", "4", "--zero_stage", "1",
+              "--warmup_steps", "1", "--log_interval", "1", "--checkpoint_dir", str(tmp_path / "ck")]
+    full = _run(common + ["--checkpoint_interval", "2"], tmp_path)
+    assert full.returncode == 0, full.stdout[-2000:] + full.stderr[-3000:]
+    names = sorted(os.listdir(tmp_path / "ck" / "step_2"))
+    assert "shard_tp0_dp0_pp0.pt" in names and "shard_tp0_dp0_pp1.pt" in names, names
+    resumed = _run(common + ["--checkpoint_interval", "1000", "--resume", str(tmp_path / "ck" / "step_2")],
+                   tmp_path)
+    assert resumed.returncode == 0, resumed.stdout[-2000:] + resumed.stderr[-3000:]
+    a, b = _losses(full.stdout), _losses(resumed.stdout)
+    assert set(b) >= {3, 4}, resumed.stdout[-1500:]
+    for s in (3, 4):
+        assert abs(a[s] - b[s]) < 1e-4, (s, a, b)
