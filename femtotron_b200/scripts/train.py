@@ -44,11 +44,13 @@ def _bool(x: str) -> bool:
 def parse_args(argv=None):
     p = argparse.ArgumentParser(description="femtotron_b200 LLaMA pretraining")
     p.add_argument("--config", type=str, default=None)
-    for k in ("dp", "tp", "pp", "zero_stage", "num_hidden_layers", "train_steps", "micro_batch_size",
+    for k in ("dp", "tp", "pp", "zero_stage", "num_hidden_layers", "hidden_size", "intermediate_size",
+              "num_attention_heads", "num_key_value_heads", "vocab_size", "max_position_embeddings",
+              "train_steps", "micro_batch_size",
               "seq_len", "warmup_steps", "num_samples", "log_interval", "checkpoint_interval",
               "grad_accum_steps", "num_microbatches", "seed"):
         p.add_argument(f"--{k}", type=int, default=None)
-    for k in ("lr", "grad_clip", "weight_decay", "min_lr_ratio", "init_std"):
+    for k in ("lr", "grad_clip", "weight_decay", "min_lr_ratio", "init_std", "rope_theta", "rms_norm_eps"):
         p.add_argument(f"--{k}", type=float, default=None)
     for k in ("zero_wrap_policy", "ac_policy", "model_name", "dataset", "checkpoint_dir", "resume",
               "schedule", "metrics_path", "data_dir", "tokenizer"):

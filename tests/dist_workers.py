@@ -1019,3 +1019,18 @@ def w_reference_bf16_parity(rank, world, ref_root, stage, steps):
         sched.step()
         theirs.append(loss.item())
     return {"ours": ours, "reference": theirs}
+
+
+# ----------------------------------------------------------------------------- export
+def w_train_and_checkpoint(rank, world, tmpdir, tp, stage):
+    """Train two steps (TP=tp, DP=world/tp, ZeRO `stage`), checkpoint at step 2, and return the
+    trained model's loss on a fixed batch."""
+    cfg = tiny_config()
+    sd = full_state(cfg)
+    ctx = ctx_of(dp=world // tp, tp=tp)
+    tr = _build_trainer(cfg, sd, ctx, stage, steps=2, mb=2, ga=1, seed_data=5, ckpt=(tmpdir, 2))
+    tr.train()
+    x = _global_batches(cfg, 1, 2, seed=8)[0]
+    with torch.no_grad():
+        loss = tr.model(x, labels=x)["loss"].item()
+    return {"loss": loss}

@@ -171,6 +171,36 @@ def test_bf16_mixed_precision_matches_reference_framework(stage):
         assert max(abs(a - b) for a, b in zip(r["ours"], r["reference"])) < 1e-2, r
 
 
+@pytest.mark.parametrize("tp,stage", [(2, 0), (1, 1), (1, 3), (2, 3)])
+def test_export_checkpoint_to_hugging_face(tp, stage, tmp_path):
+    """A Trainer checkpoint (TP and ZeRO shards) consolidates into one Hugging Face directory
+    whose LlamaForCausalLM reproduces the trained model's loss."""
+    import torch
+    from transformers import LlamaForCausalLM
+    from common_models import tiny_config
+    from femtotron_b200.models.export import export_hf
+    world = 2 * tp if stage == 3 else 2
+    res = run_ranks(W.w_train_and_checkpoint, world, str(tmp_path / "ck"), tp, stage)
+    out = export_hf(str(tmp_path / "ck" / "step_2"), tiny_config(), str(tmp_path / "hf"), dtype=torch.float32)
+    hf = LlamaForCausalLM.from_pretrained(out, torch_dtype=torch.float32)
+    x = W._global_batches(tiny_config(), 1, 2, seed=8)[0]
+    with torch.no_grad():
+        ref = hf(input_ids=x, labels=x).loss.item()
+    for r in res:
+        assert abs(r["loss"] - ref) < 1e-4, (r, ref)
+    # the command-line exporter (model shape from train.py's keys) writes the same weights
+    from femtotron_b200.scripts import export_hf as cli
+    c = tiny_config()
+    out2 = cli.main(["--checkpoint", str(tmp_path / "ck" / "step_2"), "--out", str(tmp_path / "hf2"),
+                     "--dtype", "fp32", "--hidden_size", str(c.hidden_size),
+                     "--intermediate_size", str(c.intermediate_size),
+                     "--num_attention_heads", str(c.num_attention_heads),
+                     "--num_key_value_heads", str(c.num_key_value_heads),
+                     "--num_hidden_layers", str(c.num_hidden_layers), "--vocab_size", str(c.vocab_size)])
+    hf2 = LlamaForCausalLM.from_pretrained(out2, torch_dtype=torch.float32)
+    assert all(torch.equal(a, b) for a, b in zip(hf.state_dict().values(), hf2.state_dict().values()))
+
+
 def test_zero_stages_agree():
     curves = {s: run_ranks(W.w_zero, 2, s, False)[0] for s in (0, 1, 2, 3)}
     base = curves[0]
