@@ -116,3 +116,10 @@ def test_cli_pipeline_checkpoint_resume(tmp_path):
     assert set(b) >= {3, 4}, resumed.stdout[-1500:]
     for s in (3, 4):
         assert abs(a[s] - b[s]) < 1e-4, (s, a, b)
+    # the per-stage shards also consolidate into one Hugging Face model
+    from transformers import LlamaForCausalLM
+    from femtotron_b200.scripts import export_hf
+    out = export_hf.main(["--checkpoint", str(tmp_path / "ck" / "step_2"), "--out", str(tmp_path / "hf"),
+                          "--config", cfg, "--num_hidden_layers", "2"])
+    hf = LlamaForCausalLM.from_pretrained(out)
+    assert hf.config.num_hidden_layers == 2 and len(hf.model.layers) == 2
