@@ -379,3 +379,38 @@ def test_preprocess_local_jsonl_with_byte_tokenizer(tmp_path):
     ds = PackedDataset(str(out))
     assert len(ds) == n and ds.seq_len == 8
     assert pack_tokens([[1, 2], [3]], eos=0, seq_len=3).tolist() == [[1, 2, 0]]
+
+
+def test_sampler_data_order_equals_the_reference():
+    """Data order is an interface: for the same seed, epoch and DP layout the sampler yields
+    the reference sampler's index sequence, including after a resume offset (skipped without
+    the reference)."""
+    import os
+    import sys
+    from types import SimpleNamespace
+    import pytest
+    root = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "baseline", "_ref")
+    if not os.path.isdir(os.path.join(root, "femtotron")):
+        pytest.skip("reference not installed under baseline/_ref")
+    sys.path.insert(0, root)
+    try:
+        from femtotron.data.distributed_sampler import DistributedSampler as Ref
+    finally:
+        sys.path.remove(root)
+    from femtotron_b200.data import DistributedSampler
+    for size in (7, 64, 101):
+        for dp in (1, 2, 3, 8):
+            for shuffle in (True, False):
+                for drop_last in (True, False):
+                    for r in range(dp):
+                        ctx = SimpleNamespace(dp_rank=r, dp_size=dp)
+                        a = DistributedSampler(size, ctx, seed=5, shuffle=shuffle, drop_last=drop_last)
+                        b = Ref(size, ctx, seed=5, shuffle=shuffle, drop_last=drop_last)
+                        for epoch in (0, 3):
+                            a.set_epoch(epoch)
+                            b.set_epoch(epoch)
+                            assert list(a) == list(b) and len(a) == len(b), (size, dp, r, epoch)
+                        if len(a) > 2:
+                            a.advance(2)
+                            b.advance(2)
+                            assert list(a) == list(b), (size, dp, r, "resume")
