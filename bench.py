@@ -109,8 +109,9 @@ def peaks():
 
 
 def progress(msg: str):
-    if int(os.environ.get("RANK", "0")) == 0:
-        print(f"[bench {time.strftime('%H:%M:%S')}] {msg}", file=sys.stderr, flush=True)
+    """Rank-tagged, flushed progress line on stderr (every rank), so a stop is localised."""
+    print(f"[bench r{os.environ.get('RANK', '0')} {time.strftime('%H:%M:%S')}] {msg}",
+          file=sys.stderr, flush=True)
 
 
 def emit(line: dict):
@@ -151,13 +152,13 @@ def build_ours(cfg, args, ctx, device):
 def run_ours(args):
     from collections import OrderedDict
     from femtotron_b200.data import DistributedDataLoader, SyntheticTokens, simple_pretrain_collator
-    from femtotron_b200.ops import ext
+    from femtotron_b200.ops import attention, ext
     from femtotron_b200.parallel_context import ParallelContext
     from femtotron_b200.training import Trainer
     from femtotron_b200.utils.clocks import ClockSampler
     from femtotron_b200.utils.dist import init_distributed, max_over_ranks
 
-    rank, world, local = init_distributed("nccl", timeout_s=int(os.environ.get("FT_PG_TIMEOUT", "600")))
+    rank, world, local = init_distributed("nccl", timeout_s=int(os.environ.get("FT_PG_TIMEOUT", "300")))
     device = torch.device("cuda", local)
     cfg = model_config(args.layers, args.config)
     ctx = ParallelContext(OrderedDict(tp=world) if args.tp else OrderedDict(dp=world))
@@ -195,6 +196,7 @@ def run_ours(args):
     ext.check_kernel_errors(device)
     torch.cuda.synchronize()
     dist.barrier()
+    progress("ours: timed region")
     l0 = ext.LAUNCHES[0]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     losses = []
@@ -202,7 +204,6 @@ def run_ours(args):
         torch.cuda.synchronize()
         dist.barrier()
         start.record()
-        dbg_sync = os.environ.get("FT_BENCH_SYNC") == "1"
         from femtotron_b200.utils.comm_timing import TIMER
         TIMER.collect()
         comm_tot: dict = {}
@@ -217,9 +218,6 @@ def run_ours(args):
             if TIMER.enabled:  # diagnostic mode: syncs on the step's wait events
                 for k, v in TIMER.collect().items():
                     comm_tot[k] = comm_tot.get(k, 0.0) + v
-            if dbg_sync:
-                torch.cuda.synchronize()
-                progress(f"ours: timed step {i} done")
         end.record()
         torch.cuda.synchronize()
         dist.barrier()
@@ -234,6 +232,7 @@ def run_ours(args):
     value = tokens_per_step / (ms_per_step / 1e3)
 
     # ---- end-to-end phase through the public API (pinned host -> device, loss -> host)
+    progress(f"ours: timed region done, {dev_ms / args.steps:.1f} ms/step")
     e2e = None
     if not args.no_e2e:
         ds = SyntheticTokens(num_samples=ga * mb * dp * (args.steps + 2), seq_len=S,
@@ -252,6 +251,7 @@ def run_ours(args):
         t1 = time.perf_counter()
         dist.barrier()
         e2e_ms = max_over_ranks((t1 - t0) * 1e3) / args.steps
+        progress(f"ours: end-to-end {e2e_ms:.1f} ms/step")
         e2e = {"value": tokens_per_step / (e2e_ms / 1e3), "unit": "tokens/s",
                "ms_per_step": e2e_ms,
                "h2d_bytes_per_step": ga * mb * S * 8 * 2,   # input_ids + labels, int64
@@ -278,6 +278,7 @@ def run_ours(args):
         "flops_per_token": flops_per_token(cfg, S),
         "loss_last": loss_last,
         "gpu_launches": launches,
+        "sdpa_fallbacks": attention.SDPA_FALLBACKS[0],
         "impl": "ours",
         "clocks": clk.summary(),
     }
@@ -297,8 +298,19 @@ def run_reference(args):
         return
     ref_root = os.path.join(HERE, "baseline", "_ref")
     if not os.path.isdir(os.path.join(ref_root, "femtotron")):
-        emit({"impl": "reference", "unavailable": "reference not installed under baseline/_ref"})
-        return
+        # only rank 0 installs; the others wait for the package to appear
+        if int(os.environ.get("LOCAL_RANK", "0")) == 0:
+            sys.path.insert(0, os.path.join(HERE, "baseline"))
+            try:
+                import install_reference
+                progress("reference: " + install_reference.install())
+            except Exception as e:
+                emit({"impl": "reference", "unavailable": f"reference install failed: {e!r}"[:300]})
+                return
+        else:
+            t0 = time.time()
+            while not os.path.isdir(os.path.join(ref_root, "femtotron", "training")) and time.time() - t0 < 600:
+                time.sleep(2)
     sys.path.insert(0, ref_root)
     from collections import OrderedDict
     from femtotron_b200.utils.clocks import ClockSampler

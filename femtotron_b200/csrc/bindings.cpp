@@ -38,13 +38,6 @@ void ipc_close(int64_t ptr);
 torch::Tensor tensor_at(int64_t ptr, int64_t numel, torch::ScalarType dtype, int64_t device);
 void copy_from_ptrs(const std::vector<int64_t>& dsts, const std::vector<int64_t>& srcs,
                     const std::vector<int64_t>& nbytes);
-void reduce_slices_f32(const std::vector<int64_t>& src_ptrs, torch::Tensor& acc, int64_t n,
-                       double scale, bool accumulate, bool src_f32);
-void p2p_publish(const std::vector<int64_t>& flag_ptrs, int64_t rank, int64_t epoch);
-void p2p_reduce_scatter(const std::vector<int64_t>& buf_ptrs, int64_t flags_local,
-                        const std::vector<int64_t>& flag_ptrs, torch::Tensor& acc, int64_t shard,
-                        int64_t rank, int64_t epoch, double scale, bool accumulate,
-                        torch::Tensor& err, bool src_f32, int64_t timeout_ms);
 void gemm_tc_fused(const torch::Tensor& A, const torch::Tensor& B, torch::Tensor& D, bool a_mn,
                    bool b_mn, int64_t mode,
                    const c10::optional<torch::Tensor>& R, const c10::optional<torch::Tensor>& GU,
@@ -52,7 +45,14 @@ void gemm_tc_fused(const torch::Tensor& A, const torch::Tensor& B, torch::Tensor
                    int64_t gate_epoch, int64_t gate_off, int64_t gate_row_elems,
                    int64_t gate_chunk_elems, const std::vector<int64_t>& scatter_ptrs,
                    int64_t scatter_rows);
-void stream_wait_geq(int64_t addr, int64_t value);
+void wait_flags_geq(const std::vector<int64_t>& addrs, int64_t value, torch::Tensor& err,
+                    int64_t timeout_ms, int64_t code);
+void rs_adamw(const std::vector<int64_t>& src_ptrs, int64_t base, int64_t n, bool src_f32,
+              double scale, bool accumulate, torch::Tensor& grad_shard, bool store_grad,
+              const c10::optional<torch::Tensor>& master, const c10::optional<torch::Tensor>& m,
+              const c10::optional<torch::Tensor>& v, const c10::optional<torch::Tensor>& p16,
+              const c10::optional<torch::Tensor>& segments, double beta1, double beta2,
+              double eps, int64_t step);
 void stream_write(int64_t addr, int64_t value);
 void sum_partials(const torch::Tensor& parts, const c10::optional<torch::Tensor>& resid,
                   torch::Tensor& out);
@@ -87,11 +87,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ipc_close", &ft::ipc_close);
   m.def("tensor_at", &ft::tensor_at);
   m.def("copy_from_ptrs", &ft::copy_from_ptrs);
-  m.def("p2p_reduce_scatter", &ft::p2p_reduce_scatter);
-  m.def("p2p_publish", &ft::p2p_publish);
-  m.def("reduce_slices_f32", &ft::reduce_slices_f32);
   m.def("gemm_tc_fused", &ft::gemm_tc_fused);
-  m.def("stream_wait_geq", &ft::stream_wait_geq);
+  m.def("wait_flags_geq", &ft::wait_flags_geq, "bounded wait for peer flags (one warp)");
+  m.def("rs_adamw", &ft::rs_adamw, "ZeRO reduce-scatter + fp32 cast/scale + sharded AdamW");
   m.def("stream_write", &ft::stream_write);
   m.def("sum_partials", &ft::sum_partials);
   m.def("flash_fwd", &ft::flash_fwd);

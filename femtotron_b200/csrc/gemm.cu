@@ -88,7 +88,7 @@ __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, int* er
     for (int i = 0; i < 128; ++i)
       if (mbar_try_wait(bar, parity)) return true;
     if (global_ns() - t0 > 2000000000ull) {
-      if (err) atomicExch(err, code);
+      if (err) atomicCAS(err, 0, code);   // keep the first error (the root cause)
       return false;
     }
   }
@@ -106,7 +106,7 @@ __device__ __forceinline__ bool gate_wait(const Params& p, int64_t r0, int64_t r
       asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(p.gate_flags + c) : "memory");
       if (v - p.gate_epoch >= 0) break;
       if (global_ns() - t0 > 4000000000ull) {
-        if (p.err) atomicExch(p.err, 40);
+        if (p.err) atomicCAS(p.err, 0, 40);
         return false;
       }
       __nanosleep(128);
@@ -659,6 +659,16 @@ static int num_sms() {
   return n;
 }
 
+// A gated GEMM (fused all-gather) waits for chunks that copy engines bring in after a
+// bounded wait kernel on the copy stream has seen the peers' ready flags.  A persistent grid
+// over every SM could leave that one-warp kernel no SM to run on while the GEMM waits for
+// it, so gated launches leave a few SMs free.
+constexpr int GATE_RESERVED_SMS = 4;
+
+static int usable_sms(const Params& p) {
+  return p.gate_op != 0 ? std::max(2, num_sms() - GATE_RESERVED_SMS) : num_sms();
+}
+
 template <bool A_MN, bool B_MN, int BN, int STAGES>
 static void launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, int num_tiles,
                    cudaStream_t stream) {
@@ -666,7 +676,7 @@ static void launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p
   const int smem = static_cast<int>(sizeof(Smem<BN, STAGES>)) + 1024;
   static unsigned long long configured = 0;  // per device, one mask per template instance
   smem_attr_once(kern, smem, configured);
-  const int grid = std::max(1, std::min(num_tiles, num_sms()));
+  const int grid = std::max(1, std::min(num_tiles, usable_sms(p)));
   kern<<<grid, NUM_THREADS, smem, stream>>>(ta, tb, p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
@@ -679,7 +689,7 @@ static void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUte
   const int smem = static_cast<int>(sizeof(PairSmem<PBN, STAGES>)) + 1024;
   static unsigned long long configured = 0;  // per device, one mask per template instance
   smem_attr_once(kern, smem, configured);
-  const int pairs = std::max(1, std::min(num_tiles, num_sms() / 2));
+  const int pairs = std::max(1, std::min(num_tiles, usable_sms(p) / 2));
   kern<<<2 * pairs, NUM_THREADS, smem, stream>>>(ta, tb, td, p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

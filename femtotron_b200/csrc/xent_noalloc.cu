@@ -68,42 +68,50 @@ __global__ void __launch_bounds__(512) noalloc_rows_kernel(const __nv_bfloat16* 
     float M = sm[0], S = ss[0];
     for (int i = 1; i < (int)(blockDim.x / 32); ++i) combine(M, S, sm[i], ss[i]);
     const int64_t lab = labels[row];
-    const bool valid = lab != ignore_index && lab >= 0 && lab < vocab;
+    const bool ignored = lab == ignore_index;
+    const bool valid = !ignored && lab >= 0 && lab < vocab;
     const float tgt = valid ? __bfloat162float(x[lab]) : 0.f;
-    rows_out[row] = make_float4(M, S, tgt, valid ? 1.f : 0.f);
+    // w: 1 = counted, 0 = ignored, -1 = label outside [0, vocab) (the mean becomes NaN)
+    rows_out[row] = make_float4(M, S, tgt, valid ? 1.f : (ignored ? 0.f : -1.f));
   }
 }
 
 // One block: loss = sum over valid rows of (max + log(sumexp) - target) / #valid.
 __global__ void __launch_bounds__(1024) noalloc_mean_kernel(const float4* __restrict__ rows_in,
                                                             int64_t nrows, float* __restrict__ loss_out) {
-  float acc = 0.f, cnt = 0.f;
+  float acc = 0.f, cnt = 0.f, bad = 0.f;
   for (int64_t r = threadIdx.x; r < nrows; r += blockDim.x) {
     const float4 st = rows_in[r];
-    if (st.w != 0.f) {
+    if (st.w > 0.f) {
       acc += st.x + logf(st.y) - st.z;
       cnt += 1.f;
+    } else if (st.w < 0.f) {
+      bad += 1.f;
     }
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     acc += __shfl_xor_sync(0xffffffff, acc, o);
     cnt += __shfl_xor_sync(0xffffffff, cnt, o);
+    bad += __shfl_xor_sync(0xffffffff, bad, o);
   }
-  __shared__ float sa[32], sc[32];
+  __shared__ float sa[32], sc[32], sb[32];
   const int w = threadIdx.x / 32;
   if ((threadIdx.x & 31) == 0) {
     sa[w] = acc;
     sc[w] = cnt;
+    sb[w] = bad;
   }
   __syncthreads();
   if (threadIdx.x == 0) {
-    float A = 0.f, Cn = 0.f;
+    float A = 0.f, Cn = 0.f, Bd = 0.f;
     for (int i = 0; i < (int)(blockDim.x / 32); ++i) {
       A += sa[i];
       Cn += sc[i];
+      Bd += sb[i];
     }
-    loss_out[0] = A / Cn;  // NaN when no row is valid
+    // NaN when no row is valid (a mean over an empty set) or when a label was out of range
+    loss_out[0] = Bd > 0.f ? __int_as_float(0x7fc00000) : A / Cn;
   }
 }
 
@@ -137,9 +145,11 @@ extern "C" __attribute__((visibility("default"))) int ft_xent_mean_loss_noalloc(
     const void* logits, const int64_t* labels, int64_t rows, int64_t vocab, int64_t ld,
     int64_t ignore_index, float* loss_out, void* stream) {
   if (rows > FT_XENT_NOALLOC_MAX_ROWS) return 1;
-  if (rows < 0 || logits == nullptr || labels == nullptr || loss_out == nullptr || vocab <= 0 ||
-      vocab % 8 != 0 || ld < vocab || ld % 8 != 0 || vocab > (1ll << 30) ||
-      (reinterpret_cast<uintptr_t>(logits) & 15u) != 0)
+  // with zero rows neither input is read, so they may be null (an empty tensor's pointer)
+  const bool inputs_ok = rows == 0 || (logits != nullptr && labels != nullptr &&
+                                       (reinterpret_cast<uintptr_t>(logits) & 15u) == 0);
+  if (rows < 0 || !inputs_ok || loss_out == nullptr || vocab <= 0 || vocab % 8 != 0 ||
+      ld < vocab || ld % 8 != 0 || vocab > (1ll << 30))
     return 2;
   int err = 0;
   float4* scratch = scratch_for_current_device(&err);

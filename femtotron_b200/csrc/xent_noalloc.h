@@ -14,11 +14,14 @@
 //
 // Contract:
 //   logits       bf16 [rows, ld] device pointer, 16-byte aligned; the first `vocab` columns of
-//                each row are the logits (vocab and ld multiples of 8, ld >= vocab)
-//   labels       int64 [rows] device pointer; rows whose label equals `ignore_index` are
-//                skipped; other labels must lie in [0, vocab)
-//   loss_out     float [1] device pointer: receives sum(lse - logit[label]) / (#valid rows)
-//                (NaN when no row is valid, like a mean over an empty set)
+//                each row are the logits (vocab and ld multiples of 8, ld >= vocab); may be
+//                null when rows == 0
+//   labels       int64 [rows] device pointer (may be null when rows == 0); rows whose label
+//                equals `ignore_index` are skipped; other labels must lie in [0, vocab)
+//   loss_out     float [1] device pointer: receives sum(lse - logit[label]) / (#valid rows);
+//                NaN when no row is valid (a mean over an empty set) and NaN when any label
+//                other than `ignore_index` lies outside [0, vocab), so a broken label shows
+//                as NaN instead of a plausible wrong loss
 //   stream       cudaStream_t (0 = legacy default stream)
 // Returns 0 on success; 1 if rows exceeds FT_XENT_NOALLOC_MAX_ROWS (nothing is launched);
 // 2 for an invalid argument; 3 if the one-time device set-up failed; 1000 + cudaError_t if a

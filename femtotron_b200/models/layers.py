@@ -94,8 +94,10 @@ class LlamaRotaryEmbedding(nn.Module):
 def causal_attention(qkv: torch.Tensor, B: int, S: int, nq: int, nkv: int, d: int) -> torch.Tensor:
     """Causal GQA attention over a packed [B*S, (nq+2nkv)*d] projection; returns [B*S, nq*d]."""
     from femtotron_b200.ops import attention as A
-    if qkv.is_cuda and A.USE_NATIVE and A.flash_available(d, S):
-        return A.flash_attention(qkv, B, S, nq, nkv, d)
+    if qkv.is_cuda:
+        if A.USE_NATIVE and A.flash_available(d, S):
+            return A.flash_attention(qkv, B, S, nq, nkv, d)
+        A.note_fallback(d, S)
     q = qkv[:, : nq * d].view(B, S, nq, d).transpose(1, 2)
     k = qkv[:, nq * d:(nq + nkv) * d].view(B, S, nkv, d).transpose(1, 2)
     v = qkv[:, (nq + nkv) * d:(nq + 2 * nkv) * d].view(B, S, nkv, d).transpose(1, 2)

@@ -1,19 +1,37 @@
 """Causal GQA attention entry point.
 
 ``flash_attention`` runs the sm_100a flash-attention kernels (forward and backward) on a
-packed [B*S, (nq+2nkv)*d] QKV projection.  Until those kernels are registered for a head
-size, ``flash_available`` is False and the caller uses PyTorch SDPA.
+packed [B*S, (nq+2nkv)*d] QKV projection.  They cover head sizes 64 and 128 with S a
+multiple of 128; other shapes on a GPU use PyTorch SDPA, and every such call is counted in
+``SDPA_FALLBACKS`` and announced once with a warning (FT_STRICT_ATTN=1 raises instead), so a
+benchmark or a test can assert that the library never ran on its path.
 """
 from __future__ import annotations
 
-import torch
-
 import os
+import warnings
+
+import torch
 
 from .ext import error_flag, has_native, native
 
 # FT_ATTN=sdpa routes attention to torch SDPA (for A/B measurements against the library)
 USE_NATIVE = os.environ.get("FT_ATTN", "native") != "sdpa"
+STRICT = os.environ.get("FT_STRICT_ATTN") == "1"
+# CUDA attention calls that went to PyTorch SDPA because the native kernels do not cover
+# the shape (or FT_ATTN=sdpa)
+SDPA_FALLBACKS = [0]
+
+
+def note_fallback(head_dim: int, seq_len: int) -> None:
+    """Record one CUDA attention call served by PyTorch SDPA."""
+    if STRICT and USE_NATIVE:
+        raise RuntimeError(f"native flash attention does not cover head_dim={head_dim}, "
+                           f"seq_len={seq_len} (FT_STRICT_ATTN=1)")
+    if SDPA_FALLBACKS[0] == 0 and USE_NATIVE:
+        warnings.warn(f"attention on CUDA falls back to PyTorch SDPA for head_dim={head_dim}, "
+                      f"seq_len={seq_len} (native kernels: head_dim 64/128, seq_len % 128 == 0)")
+    SDPA_FALLBACKS[0] += 1
 
 
 def flash_available(head_dim: int, seq_len: int = 128) -> bool:

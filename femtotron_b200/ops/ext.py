@@ -17,11 +17,11 @@ LAUNCHES = [0]
 
 # Kernels launched per call of an entry point when it is not exactly one: the flash backward
 # runs three (delta/LSE pre-pass, main, fp32 -> bf16 convert); the memory-management and
-# stream-memory-operation entry points launch none (copy engines, cuStreamWrite/WaitValue).
+# stream-memory-operation entry points launch none (copy engines, cuStreamWriteValue32).
 KERNELS_PER_CALL = {
     "flash_bwd": 3,
     "symm_alloc": 0, "ipc_handle": 0, "ipc_open": 0, "ipc_close": 0, "tensor_at": 0,
-    "copy_from_ptrs": 0, "stream_wait_geq": 0, "stream_write": 0,
+    "copy_from_ptrs": 0, "stream_write": 0,
 }
 
 

@@ -4,9 +4,10 @@ GPU): all-gather -> GEMM and GEMM -> reduce-scatter without SM-driven collective
 All-gather (AG) of a token-sharded activation x_local [Tl, H] into x_full [T = tp*Tl, H]:
   1. the rank stages x_local in its symmetric slot and writes epoch e into every peer's
      READY[me] flag (stream memory op, system-scope fence first);
-  2. a copy stream pulls each rank's slot (own first) with the copy engines into the local
-     x_full, each pull gated by a stream wait on READY[r] >= e and followed by a stream write
-     CHUNK[r] = e; afterwards it writes DONE[me] = e into every peer (slot may be reused);
+  2. on a copy stream a one-warp kernel waits (bounded) until every READY[r] >= e, then the
+     copy engines pull each rank's slot (own first) into the local x_full, each pull followed
+     by a stream write CHUNK[r] = e; afterwards it writes DONE[me] = e into every peer (the
+     slot may be reused);
   3. the consuming GEMM is launched on the compute stream at once: its TMA producer waits
      (bounded, in-kernel) on CHUNK[r] for the rows of each tile, so MMAs on local rows start
      while peer rows are still in flight, and each remote row crosses NVLink exactly once.
@@ -14,11 +15,17 @@ Reduce-scatter (RS) of a row-parallel GEMM's partial output over tokens:
   1. the GEMM epilogue stores every output row straight into the receive slot of the rank
      that owns that token (P2P stores over NVLink), then PART[me] = e is written to every
      owner after the GEMM;
-  2. the owner's compute stream waits for PART[r] >= e from all ranks, sums the tp partials
-     of its rows in fp32 and adds the residual in one kernel, then writes CONS[me] = e into
-     every peer so the slot can be rewritten.
+  2. the owner's compute stream waits (bounded kernel) for PART[r] >= e from all ranks, sums
+     the tp partials of its rows in fp32 and adds the residual in one kernel, then writes
+     CONS[me] = e into every peer so the slot can be rewritten.
 Slots are double-buffered per direction; epochs increase monotonically and every rank makes
 the same sequence of calls, so stale flags are never mistaken for fresh ones.
+
+Every wait is a kernel with a time limit (``wait_flags_geq``; FT_COMM_TIMEOUT_MS, default
+30 s): a peer that never publishes makes the waiting rank record an error code (200 + flag
+kind offset + peer) and continue, and the host raises KernelTimeoutError at its next
+``check_kernel_errors``.  The gated GEMM leaves a few SMs free so that the copy stream's wait
+kernel can always run while the GEMM waits for the copies it releases.
 """
 from __future__ import annotations
 
@@ -28,8 +35,14 @@ import torch.distributed as dist
 from femtotron_b200.ops.ext import error_flag, native
 from femtotron_b200.parallel.symm import SymmetricAllocator, SymmetricHeap
 
+import os
+
 KINDS = ("READY", "DONE", "PART", "CONS", "CHUNK")
 NSLOTS = 2
+# bound of every cross-rank flag wait; a peer that late has failed
+COMM_TIMEOUT_MS = int(os.environ.get("FT_COMM_TIMEOUT_MS", "30000"))
+# error code base per waited flag kind (code = base + index of the first missing peer)
+WAIT_CODES = {"READY": 200, "DONE": 220, "PART": 240, "CONS": 260}
 
 
 class TPFusedComm:
@@ -58,6 +71,11 @@ class TPFusedComm:
     def peer_flag(self, owner: int, kind: str, idx: int) -> int:
         return self.heap.peer_ptr(owner, self._flag_off(kind, idx))
 
+    def wait_all(self, kind: str, epoch: int) -> None:
+        """Bounded wait, on the current stream, until every rank's `kind` flag here >= epoch."""
+        native().wait_flags_geq([self.local_flag(kind, r) for r in range(self.world)], epoch,
+                                error_flag(self.device), COMM_TIMEOUT_MS, WAIT_CODES[kind])
+
     def fits(self, rows_local: int, cols: int) -> bool:
         return rows_local * cols <= self.slot_elems
 
@@ -72,8 +90,7 @@ class TPFusedComm:
         s = e % NSLOTS
         cur = torch.cuda.current_stream(self.device)
         if e > NSLOTS:
-            for r in range(self.world):
-                C.stream_wait_geq(self.local_flag("DONE", r), e - NSLOTS)
+            self.wait_all("DONE", e - NSLOTS)
         slot_off = self.off_ag + s * self.slot_elems * 2
         self.heap.view(slot_off, Tl * H, torch.bfloat16).copy_(x_local.reshape(-1))
         for r in range(self.world):
@@ -82,10 +99,9 @@ class TPFusedComm:
         nb = Tl * H * 2
         self.cs.wait_stream(cur)
         with torch.cuda.stream(self.cs):
+            self.wait_all("READY", e)
             for k in range(self.world):
                 r = (self.rank + k) % self.world
-                if r != self.rank:
-                    C.stream_wait_geq(self.local_flag("READY", r), e)
                 C.copy_from_ptrs([full.data_ptr() + r * nb], [self.heap.peer_ptr(r, slot_off)], [nb])
                 C.stream_write(self.local_flag("CHUNK", r), e)
             for r in range(self.world):
@@ -108,8 +124,7 @@ class TPFusedComm:
         e = self.rs_epoch = self.rs_epoch + 1
         s = e % NSLOTS
         if e > NSLOTS:
-            for r in range(self.world):
-                C.stream_wait_geq(self.local_flag("CONS", r), e - NSLOTS)
+            self.wait_all("CONS", e - NSLOTS)
         sb = self.slot_elems * 2
         ptrs = [self.heap.peer_ptr(r, self.off_rs + (s * self.world + self.rank) * sb)
                 for r in range(self.world)]
@@ -120,8 +135,7 @@ class TPFusedComm:
         s = e % NSLOTS
         for r in range(self.world):
             C.stream_write(self.peer_flag(r, "PART", self.rank), e)
-        for r in range(self.world):
-            C.stream_wait_geq(self.local_flag("PART", r), e)
+        self.wait_all("PART", e)
         sb = self.slot_elems * 2
         base = self.off_rs + s * self.world * sb
         out = torch.empty(rows_local, cols, dtype=torch.bfloat16, device=self.device)

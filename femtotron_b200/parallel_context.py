@@ -12,7 +12,7 @@ through :meth:`symmetric_heap`.
 """
 from __future__ import annotations
 
-import itertools
+import math
 from collections import OrderedDict
 
 import torch
@@ -29,21 +29,19 @@ class ParallelContext:
         self.world_rank = world_rank if world_rank is not None else dist.get_rank()
         self.dim_names = list(self.parallel_dims.keys())
         self.dim_sizes = list(self.parallel_dims.values())
-        total = 1
-        for s in self.dim_sizes:
-            total *= s
-        if total != self.world_size:
-            raise ValueError(f"product of parallel dims {total} != world_size {self.world_size}")
+        if math.prod(self.dim_sizes) != self.world_size:
+            raise ValueError(f"product of parallel dims {math.prod(self.dim_sizes)} != "
+                             f"world_size {self.world_size}")
+        # rank r sits at the row-major position of r, so the last dimension (tp) is the
+        # fastest-varying one and tensor-parallel peers are adjacent GPUs
         self.rank_grid = torch.arange(self.world_size).reshape(self.dim_sizes)
-        self.local_coord = self._rank_to_coord(self.world_rank)
+        self.local_coord = [int(c) for c in torch.nonzero(self.rank_grid == self.world_rank)[0]]
         self.groups: dict[str, dist.ProcessGroup | None] = {}
         self.ranks_in: dict[str, list[int]] = {}
         self._heaps: dict = {}
         create = dist.is_available() and dist.is_initialized()
-        for dim_idx, name in enumerate(self.dim_names):
-            group, ranks = self._create_groups_along_dim(dim_idx, create)
-            self.groups[name] = group
-            self.ranks_in[name] = ranks
+        for d, name in enumerate(self.dim_names):
+            self.groups[name], self.ranks_in[name] = self._groups_of_dim(d, create)
 
     @staticmethod
     def _normalize_parallel_dims(parallel_dims) -> "OrderedDict[str, int]":
@@ -58,26 +56,26 @@ class ParallelContext:
             out[name] = size
         return out
 
-    def _rank_to_coord(self, rank: int) -> list[int]:
-        coord = []
-        for size in reversed(self.dim_sizes):
-            coord.append(rank % size)
-            rank //= size
-        return list(reversed(coord))
+    def slices_of_dim(self, d: int) -> list[list[int]]:
+        """Every group of dimension d: moving d to the last axis makes each row of the grid
+        one set of ranks that differ only in their coordinate along d."""
+        rows = self.rank_grid.movedim(d, -1).reshape(-1, self.dim_sizes[d])
+        return [[int(r) for r in row] for row in rows]
 
-    def _create_groups_along_dim(self, dim_idx: int, create: bool):
-        my_group, my_ranks = None, None
-        ranges = [[None] if i == dim_idx else range(s) for i, s in enumerate(self.dim_sizes)]
-        for combo in itertools.product(*ranges):
-            ranks = []
-            for pos in range(self.dim_sizes[dim_idx]):
-                coord = list(combo)
-                coord[dim_idx] = pos
-                ranks.append(int(self.rank_grid[tuple(coord)].item()))
+    def _groups_of_dim(self, d: int, create: bool):
+        """(this rank's group, its ranks) along dimension d.  ``new_group`` is collective over
+        the world, so every rank creates every slice, in the same order."""
+        mine = (None, None)
+        for ranks in self.slices_of_dim(d):
             group = dist.new_group(ranks) if create else None
             if self.world_rank in ranks:
-                my_group, my_ranks = group, ranks
-        return my_group, my_ranks
+                mine = (group, ranks)
+        return mine
+
+    def _neighbor_along(self, dim_name: str, step: int) -> int | None:
+        ranks = self.ranks_in[dim_name]
+        j = ranks.index(self.world_rank) + step
+        return ranks[j] if 0 <= j < len(ranks) else None
 
     # ---------------------------------------------------------------- generic accessors
     def get_rank(self, dim_name: str) -> int:
@@ -113,20 +111,10 @@ class ParallelContext:
     def pp_group(self): return self.get_group("pp")
 
     def get_prev_rank_in(self, dim_name: str) -> int | None:
-        idx = self.dim_names.index(dim_name)
-        if self.local_coord[idx] == 0:
-            return None
-        c = list(self.local_coord)
-        c[idx] -= 1
-        return int(self.rank_grid[tuple(c)].item())
+        return self._neighbor_along(dim_name, -1)
 
     def get_next_rank_in(self, dim_name: str) -> int | None:
-        idx = self.dim_names.index(dim_name)
-        if self.local_coord[idx] == self.dim_sizes[idx] - 1:
-            return None
-        c = list(self.local_coord)
-        c[idx] += 1
-        return int(self.rank_grid[tuple(c)].item())
+        return self._neighbor_along(dim_name, +1)
 
     @property
     def pp_prev_rank(self): return self.get_prev_rank_in("pp")

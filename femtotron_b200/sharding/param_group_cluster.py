@@ -15,17 +15,22 @@ Two modes:
     their fp32 ``main_grad`` are views of flat_grad_shard, so the wgrad GEMMs accumulate
     straight into the optimizer's gradient: no gather, no scatter, no copies.
   * dp_size > 1: ``unshard`` all-gathers the packed parameters (optionally prefetched on a
-    communication stream), ``reshard`` drops them; during a unit's backward the gradients
-    go to a bf16 buffer that ``reduce_scatter_grads`` reduces (AVG) into flat_grad_shard on
-    the communication stream.
+    communication stream), ``reshard`` drops them; during a unit's backward the gradients go
+    to an unsharded buffer that ``reduce_scatter_grads`` reduces (AVG) into flat_grad_shard.
 
-With a symmetric heap (CUDA, dp > 1) the packed parameter shard and the bf16 gradient buffer
-live in IPC-shared memory: the all-gather is copy-engine pulls of every peer's shard, and the
-reduce-scatter is the native P2P kernel (publish an epoch flag to every peer after the unit's
-backward; a kernel on the communication stream waits for all peers' flags, reads its slice of
-every peer's buffer over NVLink and writes the fp32 shard, averaging and accumulating in the
-same pass).  The reference does both with NCCL collectives
-(femtotron/sharding/param_group_cluster.py:248-252, :321-324).
+With a symmetric heap (CUDA, dp > 1) the packed parameter shard and the unsharded gradient
+buffer live in IPC-shared memory:
+  * all-gather: copy-engine pulls of every peer's shard (no SM, no flag: a shard only changes
+    in the optimizer step, and every step ends with a device-side barrier);
+  * reduce-scatter: a one-element NCCL all-reduce on the reduce stream orders the ranks
+    (every rank has finished this unit's backward), then one kernel (``rs_adamw``) reads this
+    rank's slice of every peer's buffer over NVLink, averages in fp32 and writes the fp32
+    gradient shard -- and, when the optimizer allows it, applies AdamW to the shard and writes
+    the bf16 parameter shard in the same pass.  No stream or kernel ever waits on a flag
+    written by a peer, so the path cannot hang on a peer that fell behind: NCCL's own
+    collective (with the process group's timeout) is the only cross-rank wait.
+The reference does both with NCCL collectives (femtotron/sharding/param_group_cluster.py:
+248-252, :321-324) and the update as separate passes (mixed_precision_manager.py:318-331).
 """
 from __future__ import annotations
 
@@ -35,19 +40,15 @@ from torch import nn
 
 from .cluster_sharding_spec import compute_cluster_layout
 
-import os
-
-# FT_ZERO3_DEBUG_NOCOPY=1 skips the parameter transfer of every gather (wrong numerics; used
-# only to separate the cost of the transfer from the cost of its bookkeeping)
-_DEBUG_NOCOPY = os.environ.get("FT_ZERO3_DEBUG_NOCOPY") == "1"
-# bound of the in-kernel wait for the peers' gradient flags (a peer that late has failed)
-P2P_TIMEOUT_MS = int(os.environ.get("FT_P2P_TIMEOUT_MS", "20000"))
-
 
 class ParamGroupCluster:
-    def __init__(self, name: str, module: nn.Module, param_groups: list, dp_group,
+    # shard size granularity (elements) when the unit lives in symmetric memory: every slice
+    # of the fused reduce kernel starts on a 16-byte boundary
+    SYMM_ALIGN = 64
+
+    def __init__(self, name: str, module: nn.Module | None, param_groups: list, dp_group,
                  master_dtype: torch.dtype, comm_stream: torch.cuda.Stream | None = None,
-                 symm=None, symm_grad=None):
+                 symm=None, grad_offset: int | None = None):
         if not param_groups:
             raise ValueError(f"cluster {name}: empty param_groups")
         for pg in param_groups:
@@ -76,19 +77,21 @@ class ParamGroupCluster:
         # (SymmetricHeap, byte offset): flat_param_shard lives in symmetric memory and the
         # all-gather is a set of copy-engine pulls of every peer's shard (no SMs used)
         self.symm = symm
-        # (gradient buffer byte offset, flag array byte offset) in the same heap: P2P
-        # reduce-scatter instead of NCCL
-        self.symm_grad = symm_grad if symm is not None else None
-        self._rs_epoch = 0
-        # reduce-scatter flavour over the symmetric gradient buffer: "ce" (copy engines pull
-        # the peers' slices after a stream-side flag wait, then a local reduce kernel) or
-        # "p2p" (one kernel that waits for the flags and loads the peers' slices itself)
-        self.rs_mode = "ce"
+        # byte offset of the unit's unsharded gradient buffer in the same heap
+        self.grad_offset = grad_offset if symm is not None else None
+        # stream of the reduce-scatter (and of the fused update); set by the strategy
         self.rs_stream = None
         # dtype of the unsharded gradient buffer the backward accumulates into (dp > 1);
         # fp32 lets the weight-gradient GEMMs accumulate through the TMA reduce-add epilogue
         # and keeps micro-batch accumulation exact; the strategy may choose bf16 to save memory
         self.grad_dtype = self.compute_dtype
+        # kept gathered from its first use in a step until the step ends (set by the strategy)
+        self.keep = False
+        # optional callable(cluster) -> dict of fused-AdamW arguments for this step's update of
+        # the shard, or None; installed by the mixed-precision manager
+        self.early_update = None
+        # one-element tensor of the ordering collective before each reduce-scatter
+        self.order_token: torch.Tensor | None = None
 
         self.flat_param_shard = self._initialize_flat_param_shard()
         self.master = self.flat_param_shard.to(master_dtype)
@@ -105,6 +108,8 @@ class ParamGroupCluster:
         self._prefetch: tuple[torch.Tensor, torch.cuda.Event] | None = None
         self._grad_buffer: torch.Tensor | None = None
         self.in_backward = False
+        # the shard was updated early (fused with this step's reduce-scatter)
+        self.updated_early = False
         self.opt_config = dict(param_groups[0].opt_config)
         self._take_over_param_groups()
 
@@ -121,9 +126,6 @@ class ParamGroupCluster:
             return shard
         return full[s:s + self.shard_size].clone()
 
-    # shard size granularity (elements) when the unit lives in symmetric memory
-    SYMM_ALIGN = 64
-
     @staticmethod
     def shard_numel(param_groups, dp_size: int, align: int = 1) -> int:
         total = sum(pg.compute.numel() for pg in param_groups)
@@ -132,8 +134,6 @@ class ParamGroupCluster:
 
     def _gather_into(self, buf: torch.Tensor) -> None:
         """All-gather the packed parameters into `buf` on the current stream."""
-        if _DEBUG_NOCOPY:   # timing diagnostic only: bookkeeping without the transfer
-            return
         if self.symm is None:
             dist.all_gather_into_tensor(buf, self.flat_param_shard, group=self.dp_group)
             return
@@ -174,6 +174,10 @@ class ParamGroupCluster:
             ev.record(self.comm_stream)
         self._prefetch = (buf, ev)
 
+    def drop_prefetch(self) -> None:
+        """Forget a prefetched gather (its content is stale after the shards were rewritten)."""
+        self._prefetch = None
+
     def unshard(self) -> None:
         if self.direct or self._full_buffer is not None:
             return
@@ -200,18 +204,25 @@ class ParamGroupCluster:
             pg.compute.data = torch.empty(0, dtype=pg.compute.dtype, device=pg.compute.device)
         self._full_buffer = None
 
+    @property
+    def is_gathered(self) -> bool:
+        return self._full_buffer is not None
+
     # ------------------------------------------------------------------ gradients
     def prepare_grad_buffer(self) -> None:
-        """Give every parameter a bf16 ``main_grad`` view of a zeroed transient buffer
-        (dp > 1) for the upcoming backward of this unit."""
+        """Give every parameter a ``main_grad`` view of the unit's unsharded gradient buffer
+        (dp > 1) for the upcoming backward(s) of this step."""
         if self.direct or self._grad_buffer is not None:
             return
-        if self.symm_grad is not None:
+        if self.grad_offset is not None:
             # persistent symmetric buffer: every peer finished reading it in the previous
-            # step (the optimizer step is followed by a device-side barrier)
+            # step (the optimizer step ends with a device-side barrier).  No memset: the
+            # first gradient write of the step stores instead of accumulating, and the
+            # alignment padding is never written (zeroed at allocation).
             heap = self.symm[0]
-            gb = heap.view(self.symm_grad[0], self.padded_size, self.grad_dtype)
-            gb.zero_()
+            gb = heap.view(self.grad_offset, self.padded_size, self.grad_dtype)
+            for pg in self.param_groups:
+                pg.compute.grad_overwrite = True
         else:
             gb = torch.zeros(self.padded_size, dtype=self.grad_dtype, device=self.device)
         self._grad_buffer = gb
@@ -221,17 +232,25 @@ class ParamGroupCluster:
     def reduce_scatter_grads(self) -> None:
         if self.direct:
             self._grad_fresh = False
+            if self.early_update is not None and self.device.type == "cuda":
+                self._reduce_symm(None, accumulate=False)
             return
         gb = self._grad_buffer
         if gb is None:
             return
         self._grad_buffer = None
-        for pg in self.param_groups:
+        unwritten = []
+        for pg, l in zip(self.param_groups, self.layouts):
+            if getattr(pg.compute, "grad_overwrite", False):
+                unwritten.append(l)          # no gradient this step: its slice must read as 0
+                pg.compute.grad_overwrite = False
             pg.compute.main_grad = None
         fresh = self._grad_fresh
         self._grad_fresh = False
-        if self.symm_grad is not None:
-            self._p2p_reduce_scatter(accumulate=not fresh)
+        if self.grad_offset is not None:
+            for l in unwritten:
+                gb[l.global_offset:l.global_end].zero_()
+            self._reduce_symm(gb, accumulate=not fresh)
             return
         use_stream = self.comm_stream is not None and self.device.type == "cuda"
         if use_stream:
@@ -250,37 +269,36 @@ class ParamGroupCluster:
             else:
                 self.flat_grad_shard.add_(tmp.to(torch.float32))
 
-    def _p2p_reduce_scatter(self, accumulate: bool) -> None:
-        from femtotron_b200.ops.ext import error_flag, native
+    def _reduce_symm(self, gb, accumulate: bool) -> None:
+        """Reduce-scatter over the symmetric gradient buffers (dp > 1) -- or, in direct mode,
+        just the fused update of the local gradient -- on the reduce stream."""
+        from femtotron_b200.ops.ext import native
         C = native()
-        heap = self.symm[0]
-        goff, foff = self.symm_grad
-        self._rs_epoch += 1
-        ep = self._rs_epoch
-        R, rank = self.dp_size, self.dp_rank
-        flags = [heap.peer_ptr(r, foff) for r in range(R)]
         cur = torch.cuda.current_stream(self.device)
-        C.p2p_publish(flags, rank, ep)          # after this unit's backward kernels
-        st = self.rs_stream or self.comm_stream
+        st = self.rs_stream or self.comm_stream or cur
         st.wait_stream(cur)
-        f32 = self.grad_dtype == torch.float32
+        upd = self.early_update(self) if self.early_update is not None else None
+        if self.direct and upd is None:
+            return      # the gradient is already complete in flat_grad_shard
         with torch.cuda.stream(st):
-            if self.rs_mode == "p2p":
-                C.p2p_reduce_scatter([heap.peer_ptr(r, goff) for r in range(R)], flags[rank], flags,
-                                     self.flat_grad_shard, self.shard_size, rank, ep, 1.0 / R,
-                                     accumulate, error_flag(self.device), f32, P2P_TIMEOUT_MS)
-                return
-            nb = self.shard_size * (4 if f32 else 2)
-            for r in range(R):                  # peers' flags, waited in the stream (no SMs)
-                if r != rank:
-                    C.stream_wait_geq(flags[rank] + 4 * r, ep)
-            stage = torch.empty(R - 1, self.shard_size, dtype=self.grad_dtype, device=self.device)
-            peers = [r for r in range(R) if r != rank]
-            C.copy_from_ptrs([stage[i].data_ptr() for i in range(R - 1)],
-                             [heap.peer_ptr(r, goff) + rank * nb for r in peers], [nb] * (R - 1))
-            own = heap.peer_ptr(rank, goff) + rank * nb
-            C.reduce_slices_f32([own] + [stage[i].data_ptr() for i in range(R - 1)],
-                                self.flat_grad_shard, self.shard_size, 1.0 / R, accumulate, f32)
+            if self.direct:
+                srcs, base, f32, scale = [self.flat_grad_shard.data_ptr()], 0, True, 1.0
+            else:
+                # every rank has finished writing this unit's gradient buffer once this
+                # collective completes (NCCL orders it with the rank's earlier work)
+                dist.all_reduce(self.order_token, op=dist.ReduceOp.MAX, group=self.dp_group)
+                heap = self.symm[0]
+                srcs = [heap.peer_ptr(r, self.grad_offset) for r in range(self.dp_size)]
+                base, f32 = self.dp_rank * self.shard_size, self.grad_dtype == torch.float32
+                scale = 1.0 / self.dp_size
+            if upd is None:
+                C.rs_adamw(srcs, base, self.shard_size, f32, scale, accumulate, self.flat_grad_shard,
+                           True, None, None, None, None, None, 0.9, 0.999, 1e-8, 1)
+            else:
+                C.rs_adamw(srcs, base, self.shard_size, f32, scale, accumulate, self.flat_grad_shard,
+                           True, self.master, upd["exp_avg"], upd["exp_avg_sq"], self.flat_param_shard,
+                           upd["segments"], upd["beta1"], upd["beta2"], upd["eps"], upd["step"])
+                self.updated_early = True
 
     def populate_master_grad(self) -> None:
         """Point the optimizer's views at the reduced fp32 gradient (no copy)."""
@@ -300,6 +318,7 @@ class ParamGroupCluster:
         self.master.grad = None
         for v in self.param_views.values():
             v.grad = None
+        self.updated_early = False
         if self.direct:
             self.flat_grad_shard.zero_()
             self._grad_fresh = False

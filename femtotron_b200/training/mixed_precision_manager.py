@@ -16,7 +16,9 @@ B200 specifics:
 """
 from __future__ import annotations
 
+import os
 from collections import defaultdict
+from contextlib import contextmanager
 
 import torch
 from torch import nn
@@ -69,8 +71,13 @@ class MixedPrecisionManager:
         self.grad_transforms = grad_transforms or []
         self._fused_groups: set[int] = set()
         self._fused_clusters: set[int] = set()
+        # inside final_backward(): ZeRO units may apply their optimizer update fused with the
+        # gradient reduce-scatter of this (last) backward of the step
+        self._early_ok = False
         if isinstance(self.inner, FusedAdamW):
             self._register_fused_writeback()
+            if os.environ.get("FT_FUSED_RS_ADAMW", "1") != "0":
+                self._install_early_updates()
 
     # ------------------------------------------------------------------ setup helpers
     def _register_fused_writeback(self) -> None:
@@ -87,6 +94,62 @@ class MixedPrecisionManager:
         for c in self.clusters:
             if cluster_views_done[id(c)] == len(c.param_views):
                 self._fused_clusters.add(id(c))
+
+    def _install_early_updates(self) -> None:
+        """Give every CUDA cluster whose update the fused kernel can do a flat fp32 buffer
+        for each AdamW moment (the optimizer's per-view state becomes slices of it) and the
+        callback that supplies the fused update's arguments."""
+        opt = self.inner
+        group_of = {id(p): grp for grp in opt.param_groups for p in grp["params"]}
+        for c in self.clusters:
+            if c.device.type != "cuda" or id(c) not in self._fused_clusters or not c.param_views:
+                continue
+            m = torch.zeros(c.shard_size, dtype=torch.float32, device=c.device)
+            v = torch.zeros_like(m)
+            segs = []
+            for pg, l in zip(c.param_groups, c.layouts):
+                if not l.has_local_view:
+                    continue
+                t = c.param_views[pg.name]
+                opt.bind_state(t, m.narrow(0, l.local_offset, l.local_numel),
+                               v.narrow(0, l.local_offset, l.local_numel))
+                segs.append((l.local_offset, l.local_end, group_of[id(t)], t))
+            c._flat_m, c._flat_v, c._segs = m, v, segs
+            c.early_update = self._early_args
+
+    def _early_args(self, c):
+        """Arguments of the fused reduce-scatter + AdamW update of cluster c for this step, or
+        None when the update must wait for step() (outside final_backward(), gradient
+        clipping or another transform, or a second reduction of the same step)."""
+        if not self._early_ok or c.updated_early or self.grad_transforms or \
+                self.inner.grad_scale is not None:
+            return None
+        hyper = {(tuple(g["betas"]), g["eps"]) for _, _, g, _ in c._segs}
+        if len(hyper) != 1:
+            return None
+        (betas, eps), = hyper
+        step = self.inner.mark_updated([t for _, _, _, t in c._segs])
+        segs = torch.tensor([[s, e, g["lr"], g["weight_decay"]] for s, e, g, _ in c._segs],
+                            dtype=torch.float64)
+        return dict(exp_avg=c._flat_m, exp_avg_sq=c._flat_v, segments=segs, beta1=betas[0],
+                    beta2=betas[1], eps=eps, step=step)
+
+    @contextmanager
+    def final_backward(self):
+        """Wrap the last backward before ``step()``: ZeRO units whose gradients are complete
+        after it may be updated by the fused reduce-scatter + AdamW kernel right away, on
+        the reduce stream, while the rest of the backward runs."""
+        prev = self._early_ok
+        prev_s = getattr(self.strategy, "in_final_backward", None)
+        self._early_ok = True
+        if prev_s is not None:
+            self.strategy.in_final_backward = True
+        try:
+            yield
+        finally:
+            self._early_ok = prev
+            if prev_s is not None:
+                self.strategy.in_final_backward = prev_s
 
     @property
     def compute_dtype(self) -> torch.dtype:

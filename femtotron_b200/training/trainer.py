@@ -129,7 +129,7 @@ class Trainer:
         for micro in range(n):
             batch = self._batch_to_device(next(data_iter))
             last = micro == n - 1
-            ctx = nullcontext() if last else self.grad_sync.no_sync()
+            ctx = self.mp_manager.final_backward() if last else self.grad_sync.no_sync()
             with ctx:
                 TIMER.mark("fwd_last" if last else "fwd")
                 out = self.model(input_ids=batch["input_ids"], labels=batch["labels"])

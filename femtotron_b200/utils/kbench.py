@@ -221,23 +221,25 @@ def op_gemm_scatter(name):
 
 
 def op_rs_p2p(name):
-    """ZeRO-3 gradient reduce-scatter with the fp32 cast, 1/dp scale and accumulation fused:
-    one Llama-3-8B unit (218 M parameters, fp32 gradients) at DP=8, this rank's slice."""
-    from femtotron_b200.ops.ext import error_flag
+    """ZeRO-3 gradient reduce-scatter with the fp32 cast, 1/dp scale and the AdamW update of
+    the shard fused (``rs_adamw``): one Llama-3-8B unit (218 M parameters, fp32 gradients) at
+    DP=8, this rank's slice.  The eight sources are local buffers here (one GPU)."""
     R, shard = 8, 218 * 1000 * 1000 // 8 // 8 * 8
     # rank 0 reads elements [0, shard) of every peer's buffer: allocate only that slice
     bufs = [torch.randn(shard, device="cuda") for _ in range(R)]
-    flags = torch.ones(R, dtype=torch.int32, device="cuda")
-    acc = torch.zeros(shard, device="cuda")
-    err = error_flag(acc.device)
+    grad = torch.zeros(shard, device="cuda")
+    master = torch.randn(shard, device="cuda")
+    m, v = torch.zeros_like(master), torch.zeros_like(master)
+    p16 = torch.empty(shard, device="cuda", dtype=torch.bfloat16)
+    segs = torch.tensor([[0, shard, 1e-4, 0.01]], dtype=torch.float64)
     ptrs = [b.data_ptr() for b in bufs]
 
     def run():
-        native().p2p_reduce_scatter(ptrs, flags.data_ptr(), [flags.data_ptr()] * R, acc, shard, 0, 1,
-                                    1.0 / R, True, err, True, 2000)
+        native().rs_adamw(ptrs, 0, shard, True, 1.0 / R, False, grad, True, master, m, v, p16,
+                          segs, 0.9, 0.95, 1e-8, 1)
     run.keep = bufs   # the peer buffers are passed by address only
-    # read R slices + the accumulator, write the accumulator (fp32)
-    return {"kind": "bytes", "bytes": shard * 4 * (R + 2), "run": run, "name": name}
+    # read R slices + master/m/v, write grad/master/m/v (fp32) and the bf16 shard
+    return {"kind": "bytes", "bytes": shard * (4 * R + 12 + 16 + 2), "run": run, "name": name}
 
 
 OPS = {

@@ -21,3 +21,18 @@ def pytest_collection_modifyitems(config, items):
     for it in items:
         if "gpu" in it.keywords:
             it.add_marker(skip)
+
+
+@pytest.fixture(scope="session")
+def ref_root():
+    """Directory holding the unmodified reference package (``femtotron``), installed into
+    baseline/_ref on first use.  A test that needs it fails, rather than skips, when the
+    reference cannot be installed."""
+    sys.path.insert(0, os.path.join(ROOT, "baseline"))
+    try:
+        import install_reference
+    finally:
+        sys.path.pop(0)
+    if not install_reference.installed():
+        install_reference.install()
+    return install_reference.TARGET

@@ -84,11 +84,12 @@ def main():
     ctx = ParallelContext(OrderedDict(dp=dist.get_world_size()))
     z0 = train(0, ctx, cfg, sd)
     z3 = train(3, ctx, cfg, sd)
-    os.environ["FT_ZERO3_RS"] = "nccl"      # NCCL reduce-scatter for comparison
+    os.environ["FT_ZERO3_SYMM"] = "0"       # NCCL all-gather / reduce-scatter for comparison
     z3_nccl = train(3, ctx, cfg, sd)
-    os.environ["FT_ZERO3_RS"] = "p2p"       # single-kernel P2P reduce-scatter
+    os.environ.pop("FT_ZERO3_SYMM")
+    os.environ["FT_FUSED_RS_ADAMW"] = "0"   # reduce-scatter, then the optimizer at step time
     z3_p2p = train(3, ctx, cfg, sd)
-    os.environ.pop("FT_ZERO3_RS")
+    os.environ.pop("FT_FUSED_RS_ADAMW")
     t1, g1 = tp_loss(cfg, sd, 1, False)
     t2, g2 = tp_loss(cfg, sd, 2, True)
     worst = max(abs(g1[k] - g2[k]) / (g1[k] + 1e-12) for k in g1)

@@ -88,35 +88,23 @@ def test_pipeline_stage_call_order_and_state():
     assert all(r.values()), r
 
 
-def test_tiny_tp2_matches_reference_modules():
+def test_tiny_tp2_matches_reference_modules(ref_root):
     """BASELINE configuration 1 with the reference's own code as the oracle, over 100 AdamW
-    steps (skipped when the reference is not installed under baseline/_ref)."""
-    import os
-    ref_root = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "baseline", "_ref")
-    if not os.path.isdir(os.path.join(ref_root, "femtotron")):
-        pytest.skip("reference not installed under baseline/_ref")
+    steps."""
     for r in run_ranks(W.w_reference_parity, 2, ref_root, 100, timeout=900.0):
         assert len(r["ours"]) == 100
         assert max(abs(a - b) for a, b in zip(r["ours"], r["reference"])) < 1e-4, r
 
 
 @pytest.mark.parametrize("stage", [0, 1, 2, 3])
-def test_zero_training_matches_reference_framework(stage):
+def test_zero_training_matches_reference_framework(stage, ref_root):
     """DP=2 training through the reference's own MixedPrecisionManager / ZeRO strategy / LR
     schedule against this package's Trainer: same weights and batches, same loss curve."""
-    import os
-    ref_root = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "baseline", "_ref")
-    if not os.path.isdir(os.path.join(ref_root, "femtotron")):
-        pytest.skip("reference not installed under baseline/_ref")
     for r in run_ranks(W.w_reference_zero_parity, 2, ref_root, stage, 4, timeout=600.0):
         assert max(abs(a - b) for a, b in zip(r["ours"], r["reference"])) < 1e-4, r
 
 
-def test_model_state_dict_interchangeable_with_reference():
-    import os
-    ref_root = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "baseline", "_ref")
-    if not os.path.isdir(os.path.join(ref_root, "femtotron")):
-        pytest.skip("reference not installed under baseline/_ref")
+def test_model_state_dict_interchangeable_with_reference(ref_root):
     for r in run_ranks(W.w_reference_state_dict_interchange, 2, ref_root):
         assert r["same_keys"] and r["same_shapes"], r
         assert not r["missing"] and not r["unexpected"], r
@@ -124,15 +112,11 @@ def test_model_state_dict_interchangeable_with_reference():
 
 
 @pytest.mark.parametrize("stage", [0, 1, 2])
-def test_resume_from_a_reference_checkpoint(stage):
+def test_resume_from_a_reference_checkpoint(stage, ref_root):
     """A reference run's checkpoint pieces (model, MixedPrecisionManager and scheduler state
     dicts) resume in this package's trainer and continue exactly like the reference.  ZeRO-3 is
     left out: the reference does not save ZeRO-3 cluster masters, so its own runs cannot resume
     from such a checkpoint either."""
-    import os
-    ref_root = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "baseline", "_ref")
-    if not os.path.isdir(os.path.join(ref_root, "femtotron")):
-        pytest.skip("reference not installed under baseline/_ref")
     for r in run_ranks(W.w_reference_checkpoint_resume, 2, ref_root, stage, timeout=600.0):
         assert max(abs(a - b) for a, b in zip(r["ours"], r["reference"])) < 1e-5, r
 
@@ -160,13 +144,9 @@ def test_zero_state_memory_ordering():
 
 
 @pytest.mark.parametrize("stage", [0, 3])
-def test_bf16_mixed_precision_matches_reference_framework(stage):
+def test_bf16_mixed_precision_matches_reference_framework(stage, ref_root):
     """bf16 compute + fp32 masters through the reference's MixedPrecisionManager and this
     package's: 30 steps on DP=2 agree to bf16 tolerance (observed max 1.3e-3 on losses ~5.6)."""
-    import os
-    ref_root = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "baseline", "_ref")
-    if not os.path.isdir(os.path.join(ref_root, "femtotron")):
-        pytest.skip("reference not installed under baseline/_ref")
     for r in run_ranks(W.w_reference_bf16_parity, 2, ref_root, stage, 30, timeout=900.0):
         assert max(abs(a - b) for a, b in zip(r["ours"], r["reference"])) < 1e-2, r
 

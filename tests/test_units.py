@@ -219,16 +219,14 @@ def test_saved_tensor_log_diff_and_activation_checkpointing():
     assert "only in a:" in format_diff(d)
 
 
-def test_schedules_equal_the_reference_action_lists():
+def test_schedules_equal_the_reference_action_lists(ref_root):
     """The pipeline schedules are pure data: for every (P, rank, N) they must produce the same
     action sequence (compared by compact repr, e.g. F(0), SFRB(1,0)) as the reference's
-    gpipe_schedule / one_f_one_b_schedule (skipped when the reference is not installed)."""
+    gpipe_schedule / one_f_one_b_schedule ."""
     import os
     import sys
     import pytest
-    root = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "baseline", "_ref")
-    if not os.path.isdir(os.path.join(root, "femtotron")):
-        pytest.skip("reference not installed under baseline/_ref")
+    root = ref_root
     sys.path.insert(0, root)
     try:
         from femtotron.parallel.pipeline_parallel import schedule as R
@@ -246,19 +244,16 @@ def test_schedules_equal_the_reference_action_lists():
                     [repr(a) for a in R.gpipe_schedule(N, first, last)], (P, rank, N)
 
 
-def test_cluster_layout_equals_the_reference():
+def test_cluster_layout_equals_the_reference(ref_root):
     """compute_cluster_layout keeps the reference's flat, padded-to-dp layout (so ZeRO-3
     shards and checkpoints line up): every field of every parameter's spec, the shard size and
-    the padding agree for assorted parameter lists and DP sizes (skipped when the reference is
-    not installed)."""
+    the padding agree for assorted parameter lists and DP sizes."""
     import os
     import random
     import sys
     import pytest
     import torch
-    root = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "baseline", "_ref")
-    if not os.path.isdir(os.path.join(root, "femtotron")):
-        pytest.skip("reference not installed under baseline/_ref")
+    root = ref_root
     sys.path.insert(0, root)
     try:
         from femtotron.sharding.cluster_sharding_spec import compute_cluster_layout as ref_layout
@@ -282,18 +277,16 @@ def test_cluster_layout_equals_the_reference():
                 assert all(getattr(x, f) == getattr(y, f) for f in fields), (trial, rank, x, y)
 
 
-def test_lr_schedule_and_param_groups_equal_the_reference():
+def test_lr_schedule_and_param_groups_equal_the_reference(ref_root):
     """The LR multiplier (linear warm-up with the reference's current_step+1 shift, cosine to
     min_lr_ratio) and the weight-decay grouping equal the reference's for the same inputs
-    (skipped when the reference is not installed)."""
+    ."""
     import os
     import sys
     import pytest
     import torch
     from common_models import tiny_config
-    root = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "baseline", "_ref")
-    if not os.path.isdir(os.path.join(root, "femtotron")):
-        pytest.skip("reference not installed under baseline/_ref")
+    root = ref_root
     sys.path.insert(0, root)
     try:
         from femtotron.training.lr_schedule import create_lr_schedule as ref_lr
@@ -323,19 +316,16 @@ def test_lr_schedule_and_param_groups_equal_the_reference():
         assert [names[id(p)] for p in a["params"]] == [names[id(p)] for p in b["params"]]
 
 
-def test_reference_import_paths_and_public_names_exist():
+def test_reference_import_paths_and_public_names_exist(ref_root):
     """Every module of the reference package has a same-path module here
     (femtotron.X.Y -> femtotron_b200.X.Y), and every public top-level class and function of the
     reference module exists in it, so code written against the reference's imports resolves.
-    The reference's names are read from its source (no import); skipped without it."""
+    The reference's names are read from its source (no import)."""
     import ast
     import importlib
     import os
-    import pytest
-    root = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "baseline", "_ref")
+    root = ref_root
     pkg = os.path.join(root, "femtotron")
-    if not os.path.isdir(pkg):
-        pytest.skip("reference not installed under baseline/_ref")
     missing = []
     for dirpath, _, files in os.walk(pkg):
         if f"{os.sep}test" in dirpath[len(pkg):]:
@@ -381,17 +371,14 @@ def test_preprocess_local_jsonl_with_byte_tokenizer(tmp_path):
     assert pack_tokens([[1, 2], [3]], eos=0, seq_len=3).tolist() == [[1, 2, 0]]
 
 
-def test_sampler_data_order_equals_the_reference():
+def test_sampler_data_order_equals_the_reference(ref_root):
     """Data order is an interface: for the same seed, epoch and DP layout the sampler yields
-    the reference sampler's index sequence, including after a resume offset (skipped without
-    the reference)."""
+    the reference sampler's index sequence, including after a resume offset."""
     import os
     import sys
     from types import SimpleNamespace
     import pytest
-    root = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "baseline", "_ref")
-    if not os.path.isdir(os.path.join(root, "femtotron")):
-        pytest.skip("reference not installed under baseline/_ref")
+    root = ref_root
     sys.path.insert(0, root)
     try:
         from femtotron.data.distributed_sampler import DistributedSampler as Ref
@@ -414,3 +401,39 @@ def test_sampler_data_order_equals_the_reference():
                             a.advance(2)
                             b.advance(2)
                             assert list(a) == list(b), (size, dp, r, "resume")
+
+
+def test_parallel_context_groups_match_coordinate_enumeration():
+    """Every group of every dimension holds exactly the ranks whose row-major coordinates
+    differ from this rank's only along that dimension, in coordinate order (tp innermost);
+    prev/next ranks are the neighbours in that order."""
+    from collections import OrderedDict
+    from femtotron_b200.parallel_context import SUPPORTED_PARALLEL_DIMS, ParallelContext
+    for dims in [dict(pp=2, dp=2, tp=2), dict(dp=4), dict(pp=3, dp=2, tp=4), dict(tp=8),
+                 dict(pp=2, cp=2, tp=2), dict(pp=2, dp=3)]:
+        sizes = [dims.get(n, 1) for n in SUPPORTED_PARALLEL_DIMS]
+        world = 1
+        for s in sizes:
+            world *= s
+        for rank in range(world):
+            ctx = ParallelContext(OrderedDict(dims), world_size=world, world_rank=rank)
+            coord, r = [], rank
+            for s in reversed(sizes):
+                coord.append(r % s)
+                r //= s
+            coord.reverse()
+            assert ctx.local_coord == coord
+            for d, name in enumerate(SUPPORTED_PARALLEL_DIMS):
+                want = []
+                for pos in range(sizes[d]):
+                    c = list(coord)
+                    c[d] = pos
+                    idx = 0
+                    for s, x in zip(sizes, c):
+                        idx = idx * s + x
+                    want.append(idx)
+                assert ctx.get_ranks_in_group(name) == want
+                assert ctx.get_rank(name) == coord[d]
+                i = want.index(rank)
+                assert ctx.get_prev_rank_in(name) == (want[i - 1] if i > 0 else None)
+                assert ctx.get_next_rank_in(name) == (want[i + 1] if i + 1 < len(want) else None)
