@@ -1,68 +1,88 @@
-"""Headline benchmark: Llama-3-8B training throughput (tokens/s for the whole job + MFU) with
-ZeRO-3 data parallelism over N B200 GPUs of one node, seq 4096, micro-batch 1, gradient
-accumulation 8, full activation checkpointing, bf16 compute with fp32 master weights and
-AdamW; synthetic uniform token ids and random-init weights.
+"""Training-throughput benchmark of the BASELINE configurations (tokens/s for the whole job +
+MFU), one process per GPU of one node; synthetic uniform token ids, random-init weights.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py [--config NAME] [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
     torchrun --nproc-per-node N --master-addr 127.0.0.1 bench.py --gpus N ...
 
-Per step each GPU processes grad_accum x micro_batch x seq tokens (weak scaling).
+Configurations (``--config``; the default is the headline):
+  llama3-8b-zero3       Llama-3-8B, ZeRO-3 over all N GPUs, seq 4096, micro-batch 1, grad-accum
+                        8, full activation checkpointing (weak scaling: fixed work per GPU)
+  llama2-13b-tp-sp      Llama-2-13B, tensor parallel over all N GPUs with sequence parallelism,
+                        DP=1, seq 4096, micro-batch 2 (strong scaling); the reference has no
+                        sequence parallelism, so its arm runs plain tensor parallelism
+  llama2-7b-3d          Llama-2-7B, TP=2 x PP=2 x DP=N/4 with ZeRO-1, 1F1B over 8 micro-batches
+                        of 1 x seq 2048 (N a multiple of 4; weak scaling over DP)
+  llama3-70b-tp4-zero3  Llama-3-70B, TP=4 x ZeRO-3 DP=N/4, seq 4096, micro-batch 1,
+                        grad-accum 16, full activation checkpointing (N a multiple of 4)
 
-Two measurements of our implementation, each over K steps after W warm-up steps:
+Every configuration is built through the public training entry point
+(``femtotron_b200.scripts.train.build_all`` with the YAML under configs/), bf16 compute with
+fp32 master weights and AdamW.  Two measurements, each over K steps after W warm-up steps:
   * ``value``: device time (CUDA events on the compute stream, barrier + synchronize on both
-    sides, max over ranks) of K steps with the micro-batches already on the device;
-  * ``e2e``: K steps through the public API (Trainer.train_step over a DistributedDataLoader):
-    every step copies its token ids from pinned host memory to the device and reads the
-    loss back to the host; host wall clock, max over ranks.
-The per-step working set (weights, optimizer state, activations: >100 GB) exceeds the 126 MB
-L2 cache, so no explicit L2 flush is needed between steps.
+    sides, max over ranks) of K optimizer steps whose micro-batches are already on the device;
+  * ``e2e``: K steps through ``Trainer.train_step`` over the DistributedDataLoader: every step
+    copies its token ids from pinned host memory to the device and reads the loss back to the
+    host; host wall clock, max over ranks.
+The per-step working set (weights, optimizer state, activations: tens of GB) exceeds the
+126 MB L2 cache, so no explicit flush is needed between steps.
 
-``--config llama2-13b-tp-sp`` measures the secondary BASELINE configuration instead: Llama-2-13B
-with tensor parallelism over all N GPUs plus sequence parallelism (DP=1, micro-batch 2,
-seq 4096, no activation checkpointing; strong scaling).
-
-``--impl reference`` runs the unmodified reference (installed under baseline/_ref) through
-its own public API on the same configuration and prints the same JSON line with
-"impl": "reference".
+``--impl reference`` runs the unmodified reference (installed under baseline/_ref on first
+use) through its own public API and stock training step on the same configuration and prints
+the same JSON line with "impl": "reference".
 """
 from __future__ import annotations
 
 import argparse
+import contextlib
 import json
 import os
 import sys
 import time
-import traceback
 
+import femtotron_b200  # noqa: F401  (sets the stream/queue environment before CUDA starts)
 import torch
 import torch.distributed as dist
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 METRIC = "tokens/sec/box + MFU, Llama-3-8B ZeRO-3 & TP=8, 1/2/4/8 B200, max over ranks"
 
-LLAMA3_8B = dict(hidden_size=4096, intermediate_size=14336, num_attention_heads=32,
-                 num_key_value_heads=8, num_hidden_layers=32, vocab_size=128256,
-                 max_position_embeddings=8192, rms_norm_eps=1e-5, rope_theta=500000.0,
-                 tie_word_embeddings=False)
+
+def _layout_dp(w):
+    return 1, w, 1
 
 
-LLAMA2_13B = dict(hidden_size=5120, intermediate_size=13824, num_attention_heads=40,
-                  num_key_value_heads=40, num_hidden_layers=40, vocab_size=32000,
-                  max_position_embeddings=4096, rms_norm_eps=1e-5, rope_theta=10000.0,
-                  tie_word_embeddings=False)
+def _layout_tp(w):
+    return 1, 1, w
 
-# --config: the default is the headline benchmark; the others are secondary BASELINE configs
+
+def _layout_3d(w):
+    if w % 4:
+        raise ValueError("llama2-7b-3d needs a multiple of 4 GPUs (TP=2 x PP=2 x DP)")
+    return 2, w // 4, 2
+
+
+def _layout_tp4(w):
+    if w % 4:
+        raise ValueError("llama3-70b-tp4-zero3 needs a multiple of 4 GPUs (TP=4 x DP)")
+    return 1, w // 4, 4
+
+
+# per configuration: YAML, model name, (pp, dp, tp) for N GPUs, and the scaling kind
 CONFIGS = {
-    "llama3-8b-zero3": dict(model=LLAMA3_8B, name="Llama-3-8B", micro_batch=1, grad_accum=8, seq=4096),
-    "llama2-13b-tp-sp": dict(model=LLAMA2_13B, name="Llama-2-13B", micro_batch=2, grad_accum=1, seq=4096),
+    "llama3-8b-zero3": dict(yaml="llama3_8b_zero3.yaml", name="Llama-3-8B", layout=_layout_dp,
+                            scaling="weak"),
+    "llama2-13b-tp-sp": dict(yaml="llama2_13b_tp8_sp.yaml", name="Llama-2-13B", layout=_layout_tp,
+                             scaling="strong"),
+    "llama2-7b-3d": dict(yaml="llama2_7b_3d.yaml", name="Llama-2-7B", layout=_layout_3d,
+                         scaling="weak"),
+    "llama3-70b-tp4-zero3": dict(yaml="llama3_70b_tp4_zero3.yaml", name="Llama-3-70B",
+                                 layout=_layout_tp4, scaling="weak"),
 }
 
 
 def parse():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--config", default="llama3-8b-zero3", choices=sorted(CONFIGS),
-                    help="llama3-8b-zero3: ZeRO-3 over all GPUs (headline); llama2-13b-tp-sp: "
-                         "tensor parallel over all GPUs with sequence parallelism, DP=1")
+    ap.add_argument("--config", default="llama3-8b-zero3", choices=sorted(CONFIGS))
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
@@ -73,31 +93,53 @@ def parse():
     ap.add_argument("--layers", type=int, default=None,
                     help="override layer count (debug only; results are then not the benchmark)")
     ap.add_argument("--no-e2e", action="store_true")
-    args = ap.parse_args()
+    return ap.parse_args()
+
+
+def bench_cfg(args, world: int) -> dict:
+    """The training configuration of the benchmark: the entry point's defaults <- the YAML of
+    the configuration <- the benchmark's settings (layout for N GPUs, no clipping, synthetic
+    data large enough for every step)."""
+    import yaml
+    from femtotron_b200.scripts.train import DEFAULTS
     c = CONFIGS[args.config]
-    args.seq = args.seq or c["seq"]
-    args.micro_batch = args.micro_batch or c["micro_batch"]
-    args.grad_accum = args.grad_accum or c["grad_accum"]
-    args.tp = args.config == "llama2-13b-tp-sp"
-    args.model_name = c["name"]
-    return args
-
-
-def model_config(layers=None, config="llama3-8b-zero3"):
-    from transformers import LlamaConfig
-    kw = dict(CONFIGS[config]["model"])
-    if layers:
-        kw["num_hidden_layers"] = layers
-    cfg = LlamaConfig(**kw)
-    cfg.use_cache = False
+    cfg = dict(DEFAULTS)
+    with open(os.path.join(HERE, "configs", c["yaml"])) as f:
+        cfg.update(yaml.safe_load(f) or {})
+    pp, dp, tp = c["layout"](world)
+    cfg.update(pp=pp, dp=dp, tp=tp)
+    if args.seq:
+        cfg["seq_len"] = args.seq
+    if args.micro_batch:
+        cfg["micro_batch_size"] = args.micro_batch
+    if args.grad_accum:
+        cfg["grad_accum_steps"] = args.grad_accum
+    if args.layers:
+        cfg["num_hidden_layers"] = args.layers
+    cfg["max_position_embeddings"] = max(cfg["max_position_embeddings"], cfg["seq_len"])
+    total = args.warmup + 2 * args.steps + 10
+    rows = cfg["micro_batch_size"] * (cfg["num_microbatches"] if pp > 1 else 1)
+    cfg.update(grad_clip=None, train_steps=total, warmup_steps=2, lr=3e-4, min_lr_ratio=0.1,
+               log_interval=10 ** 9, checkpoint_interval=10 ** 9, synthetic_data=True,
+               num_samples=cfg["grad_accum_steps"] * rows * dp * (args.steps + args.warmup + 4),
+               init_std=0.02, seed=1234, metrics_path=None, ac_preserve_rng_state=False,
+               _explicit=set())
+    cfg["_rows"] = rows
     return cfg
 
 
-def flops_per_token(cfg, seq) -> float:
+def model_config(cfg):
+    from femtotron_b200.scripts.train import model_config_from
+    mc = model_config_from(cfg)
+    mc.use_cache = False
+    return mc
+
+
+def flops_per_token(mc, seq) -> float:
     """Model FLOPs per trained token: 6 x (matmul parameters) + 6 x L x H x S for causal
     attention (score and value products, forward+backward).  Recomputation is not counted."""
     from femtotron_b200.utils.flops import llama_flops_per_token
-    return llama_flops_per_token(cfg, seq)
+    return llama_flops_per_token(mc, seq)
 
 
 def peaks():
@@ -119,74 +161,71 @@ def emit(line: dict):
         print(json.dumps(line), flush=True)
 
 
+def describe(args, cfg) -> dict:
+    pp, dp, tp = cfg["pp"], cfg["dp"], cfg["tp"]
+    c = CONFIGS[args.config]
+    par = f"zero{cfg['zero_stage']}-dp{dp}"
+    if tp > 1:
+        par = f"tp{tp}" + ("-sp" if cfg.get("sequence_parallel") else "") + (f"-{par}" if dp > 1 else "")
+    if pp > 1:
+        par = f"pp{pp}-{cfg['schedule']}-{par}"
+    model = c["name"] if not args.layers else f"{c['name']}-{args.layers}L(debug)"
+    return {"model": model, "global_batch": cfg["grad_accum_steps"] * cfg["_rows"] * dp,
+            "micro_batch": cfg["micro_batch_size"], "grad_accum": cfg["grad_accum_steps"],
+            "pipeline_microbatches": cfg["num_microbatches"] if pp > 1 else None,
+            "seq_len": cfg["seq_len"], "parallelism": par,
+            "activation_checkpointing": "full" if cfg["ac_enabled"] else "none",
+            "optimizer": "AdamW fp32 master",
+            "l2": "per-step working set (weights, optimizer state, activations) >> 126 MB L2 (no flush needed)"}
+
+
 # ----------------------------------------------------------------------------- our arm
-def build_ours(cfg, args, ctx, device):
-    from femtotron_b200.models import build_llama_model, get_llama_parallel_plan, materialize_model
-    from femtotron_b200.parallel.data_parallel import create_grad_synchronizer
-    from femtotron_b200.sharding import ZeROConfig, create_sharding_strategy, llama_wrap_policy
-    from femtotron_b200.training import (FusedAdamW, MixedPrecisionManager, TrainConfig,
-                                         apply_activation_checkpointing, create_lr_schedule,
-                                         get_param_groups)
-    from femtotron_b200.training.ckpt_policy import by_class
-    from femtotron_b200.models.layers import LlamaDecoderLayer
-    torch.manual_seed(1234)
-    model = build_llama_model(cfg, ctx, sequence_parallel=args.tp and ctx.tp_size > 1)
-    materialize_model(model, device, dtype=torch.bfloat16, init_std=0.02)
-    total_steps = args.warmup + 2 * args.steps + 10
-    tc = TrainConfig(train_steps=total_steps, grad_accum_steps=args.grad_accum, grad_clip=None,
-                     master_dtype=torch.float32, param_dtype=torch.bfloat16, log_interval=10 ** 9,
-                     checkpoint_interval=10 ** 9, warmup_steps=2, lr=3e-4)
-    zc = ZeROConfig(stage=0) if args.tp else ZeROConfig(stage=3, wrap_policy=llama_wrap_policy)
-    strategy = create_sharding_strategy(ctx, zc)
-    mp = MixedPrecisionManager(model, ctx, get_llama_parallel_plan(), tc, FusedAdamW,
-                               dict(lr=3e-4, betas=(0.9, 0.95), eps=1e-8),
-                               get_param_groups(model, 0.01), sharding_strategy=strategy)
-    if not args.tp:   # the ZeRO-3 config trains with full activation checkpointing
-        apply_activation_checkpointing(model, by_class(LlamaDecoderLayer), use_reentrant=False,
-                                       preserve_rng_state=False)
-    sched = create_lr_schedule(mp.inner, tc.warmup_steps, total_steps, 0.1)
-    gsync = create_grad_synchronizer(mp.groups, ctx, strategy)
-    return model, mp, sched, gsync, tc
-
-
 def run_ours(args):
-    from collections import OrderedDict
-    from femtotron_b200.data import DistributedDataLoader, SyntheticTokens, simple_pretrain_collator
     from femtotron_b200.ops import attention, ext
-    from femtotron_b200.parallel_context import ParallelContext
-    from femtotron_b200.training import Trainer
+    from femtotron_b200.scripts.train import build_all
     from femtotron_b200.utils.clocks import ClockSampler
+    from femtotron_b200.utils.comm_timing import TIMER
     from femtotron_b200.utils.dist import init_distributed, max_over_ranks
 
     rank, world, local = init_distributed("nccl", timeout_s=int(os.environ.get("FT_PG_TIMEOUT", "300")))
     device = torch.device("cuda", local)
-    cfg = model_config(args.layers, args.config)
-    ctx = ParallelContext(OrderedDict(tp=world) if args.tp else OrderedDict(dp=world))
-    model, mp, sched, gsync, tc = build_ours(cfg, args, ctx, device)
-    ga, mb, S = args.grad_accum, args.micro_batch, args.seq
+    cfg = bench_cfg(args, world)
+    mc = model_config(cfg)
+    progress(f"ours: building {args.config} pp={cfg['pp']} dp={cfg['dp']} tp={cfg['tp']}")
+    with contextlib.redirect_stdout(sys.stderr):   # stdout carries only the JSON line
+        trainer = build_all(cfg)
+    mp, sched = trainer.mp_manager, trainer.scheduler
+    ctx = trainer.parallel_ctx
+    ga, rows, S, dp = cfg["grad_accum_steps"], cfg["_rows"], cfg["seq_len"], cfg["dp"]
 
-    # ---- device-timed phase: micro-batches pre-staged on the device
+    # ---- device-timed phase: the step's micro-batches pre-staged on the device
     g = torch.Generator(device="cpu")
-    g.manual_seed(1000 + ctx.dp_rank)   # tensor-parallel peers share their batch
-    dev_batches = [torch.randint(0, cfg.vocab_size, (mb, S), generator=g).to(device) for _ in range(ga)]
+    g.manual_seed(1000 + ctx.dp_rank)   # tensor- and pipeline-parallel peers share their batch
+    dev_batches = [torch.randint(0, mc.vocab_size, (rows, S), generator=g).to(device) for _ in range(ga)]
 
     class DevIter:
+        i = -1
+
         def __iter__(self):
             return self
 
         def __next__(self):
-            self.i = getattr(self, "i", -1) + 1
+            self.i += 1
             x = dev_batches[self.i % ga]
             return {"input_ids": x, "labels": x}
 
-    class Null:
-        micro_batch_size = mb
-        dataset = None
+    def device_step(it):
+        if trainer.pp_runner is None:
+            loss = trainer._train_one_step_standard(it)
+        else:
+            loss = trainer._train_one_step_pp(it)
+        TIMER.mark("optimizer")
+        trainer.grad_sync.sync_gradients()
+        mp.step()
+        sched.step()
+        TIMER.mark(None)
+        return loss
 
-        def set_epoch(self, e):
-            pass
-
-    trainer = Trainer(model, mp, sched, Null(), gsync, ctx, tc)
     mp.strategy.prepare_for_backward(mp.groups)
     it = DevIter()
     progress("ours: model built, starting warm-up")
@@ -200,21 +239,14 @@ def run_ours(args):
     l0 = ext.LAUNCHES[0]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     losses = []
+    comm_tot: dict = {}
     with ClockSampler(local) as clk:
         torch.cuda.synchronize()
         dist.barrier()
-        start.record()
-        from femtotron_b200.utils.comm_timing import TIMER
         TIMER.collect()
-        comm_tot: dict = {}
+        start.record()
         for i in range(args.steps):
-            info = trainer._train_one_step_standard(it)
-            TIMER.mark("optimizer")
-            trainer.grad_sync.sync_gradients()
-            mp.step()
-            sched.step()
-            TIMER.mark(None)
-            losses.append(info)
+            losses.append(device_step(it))
             if TIMER.enabled:  # diagnostic mode: syncs on the step's wait events
                 for k, v in TIMER.collect().items():
                     comm_tot[k] = comm_tot.get(k, 0.0) + v
@@ -222,25 +254,19 @@ def run_ours(args):
         torch.cuda.synchronize()
         dist.barrier()
     launches = ext.LAUNCHES[0] - l0
-    dev_ms = start.elapsed_time(end)
-    dev_ms = max_over_ranks(dev_ms)
+    dev_ms = max_over_ranks(start.elapsed_time(end))
     loss_last = float(losses[-1].item())
     ext.check_kernel_errors(device)
     ms_per_step = dev_ms / args.steps
-    dp = ctx.dp_size
-    tokens_per_step = ga * mb * S * dp
+    tokens_per_step = ga * rows * S * dp
     value = tokens_per_step / (ms_per_step / 1e3)
+    progress(f"ours: timed region done, {ms_per_step:.1f} ms/step")
 
     # ---- end-to-end phase through the public API (pinned host -> device, loss -> host)
-    progress(f"ours: timed region done, {dev_ms / args.steps:.1f} ms/step")
     e2e = None
     if not args.no_e2e:
-        ds = SyntheticTokens(num_samples=ga * mb * dp * (args.steps + 2), seq_len=S,
-                             vocab_size=cfg.vocab_size, seed=7)
-        dl = DistributedDataLoader(ds, ctx, mb, simple_pretrain_collator, num_workers=2, pin_memory=True)
-        trainer.dataloader = dl
-        dl.set_epoch(0)
-        it2 = iter(dl)
+        trainer.dataloader.set_epoch(0)
+        it2 = iter(trainer.dataloader)
         trainer.train_step(it2)  # warm the loader workers
         torch.cuda.synchronize()
         dist.barrier()
@@ -254,31 +280,29 @@ def run_ours(args):
         progress(f"ours: end-to-end {e2e_ms:.1f} ms/step")
         e2e = {"value": tokens_per_step / (e2e_ms / 1e3), "unit": "tokens/s",
                "ms_per_step": e2e_ms,
-               "h2d_bytes_per_step": ga * mb * S * 8 * 2,   # input_ids + labels, int64
-               "d2h_bytes_per_step": 4}                     # fp32 loss
+               # input_ids + labels (int64) of this rank's micro-batches; the fp32 loss back
+               "h2d_bytes_per_step": ga * rows * S * 8 * 2,
+               "d2h_bytes_per_step": 4}
 
     pk = peaks()
-    mfu = value * flops_per_token(cfg, S) / (world * pk["bf16_tflops"] * 1e12)
+    mfu = value * flops_per_token(mc, S) / (world * pk["bf16_tflops"] * 1e12)
     exposed = None
     if comm_tot:
-        # compute-stream time blocked on communication, per step, max over ranks
+        # compute-stream time blocked on communication, and per-phase device time, per step,
+        # max over ranks
         exposed = {k: round(max_over_ranks(v) / args.steps, 2) for k, v in sorted(comm_tot.items())}
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 2),
-        "higher_is_better": True, "scaling": "strong" if args.tp else "weak", "vs_baseline": None,
+        "higher_is_better": True, "scaling": CONFIGS[args.config]["scaling"], "vs_baseline": None,
         "dtype": "bf16", "data": "synthetic (uniform random token ids, random-init weights)",
-        "config": {"model": args.model_name if not args.layers else f"{args.model_name}-{args.layers}L(debug)",
-                   "global_batch": ga * mb * dp, "micro_batch": mb, "grad_accum": ga,
-                   "seq_len": S,
-                   "parallelism": f"tp{world}-sp" if args.tp else f"zero3-dp{world}",
-                   "activation_checkpointing": "none" if args.tp else "full",
-                   "optimizer": "AdamW fp32 master", "l2": "per-step working set (weights, optimizer state, activations) >> 126 MB L2 (no flush needed)"},
+        "config": describe(args, cfg),
         "mfu": round(mfu, 4), "mfu_peak_tflops": pk["bf16_tflops"],
-        "flops_per_token": flops_per_token(cfg, S),
+        "flops_per_token": flops_per_token(mc, S),
         "loss_last": loss_last,
         "gpu_launches": launches,
         "sdpa_fallbacks": attention.SDPA_FALLBACKS[0],
+        "peak_mem_gb": round(max_over_ranks(torch.cuda.max_memory_allocated(device) / 2 ** 30), 1),
         "impl": "ours",
         "clocks": clk.summary(),
     }
@@ -292,30 +316,39 @@ def run_ours(args):
 
 
 # ----------------------------------------------------------------------------- reference arm
+def _install_reference(ref_root: str) -> str | None:
+    """Returns None when the reference is importable from ref_root, else the reason."""
+    if os.path.isdir(os.path.join(ref_root, "femtotron", "training")):
+        return None
+    # only one process installs; the others wait for the package to appear
+    if int(os.environ.get("LOCAL_RANK", "0")) == 0:
+        sys.path.insert(0, os.path.join(HERE, "baseline"))
+        try:
+            import install_reference
+            progress("reference: " + install_reference.install())
+        except Exception as e:
+            return f"reference install failed: {e!r}"[:300]
+        finally:
+            sys.path.pop(0)
+    else:
+        t0 = time.time()
+        while not os.path.isdir(os.path.join(ref_root, "femtotron", "training")) and time.time() - t0 < 600:
+            time.sleep(2)
+    return None if os.path.isdir(os.path.join(ref_root, "femtotron", "training")) else \
+        "reference not installed under baseline/_ref"
+
+
 def run_reference(args):
-    if args.config != "llama3-8b-zero3":
-        emit({"impl": "reference", "unavailable": "the reference arm covers the headline configuration only"})
-        return
     ref_root = os.path.join(HERE, "baseline", "_ref")
-    if not os.path.isdir(os.path.join(ref_root, "femtotron")):
-        # only rank 0 installs; the others wait for the package to appear
-        if int(os.environ.get("LOCAL_RANK", "0")) == 0:
-            sys.path.insert(0, os.path.join(HERE, "baseline"))
-            try:
-                import install_reference
-                progress("reference: " + install_reference.install())
-            except Exception as e:
-                emit({"impl": "reference", "unavailable": f"reference install failed: {e!r}"[:300]})
-                return
-        else:
-            t0 = time.time()
-            while not os.path.isdir(os.path.join(ref_root, "femtotron", "training")) and time.time() - t0 < 600:
-                time.sleep(2)
+    why = _install_reference(ref_root)
+    if why is not None:
+        emit({"impl": "reference", "unavailable": why})
+        return
     sys.path.insert(0, ref_root)
     from collections import OrderedDict
     from femtotron_b200.utils.clocks import ClockSampler
     from femtotron_b200.utils.dist import init_distributed, max_over_ranks
-    rank, world, local = init_distributed("nccl")
+    rank, world, local = init_distributed("nccl", timeout_s=int(os.environ.get("FT_PG_TIMEOUT", "600")))
     device = torch.device("cuda", local)
     try:
         from femtotron.parallel_context import ParallelContext as RCtx
@@ -331,49 +364,71 @@ def run_reference(args):
         from femtotron.sharding.zero_config import ZeROConfig as RZ
         from femtotron.scripts.presets import get_wrap_policy, get_ac_policy
         from femtotron.parallel.data_parallel.gradient_synchronizer import create_grad_synchronizer as rsync
+        from femtotron.parallel.pipeline_parallel.comm_ops import PipelineComm as RComm
+        from femtotron.parallel.pipeline_parallel.runner import PipelineRunner as RRunner
+        from femtotron.parallel.pipeline_parallel.stage import PipelineStage as RStage
+        from femtotron.parallel.pipeline_parallel.partition import partition_layers as rpart
+        from femtotron.parallel.pipeline_parallel.pipeline_config import PipelineConfig as RPC
         from femtotron.data.data_loader import DistributedDataLoader as RDL
         from femtotron.data.collator import simple_pretrain_collator as rcoll
     except Exception as e:  # pragma: no cover
         emit({"impl": "reference", "unavailable": f"reference import failed: {e!r}"[:300]})
         return
-    cfg = model_config(args.layers)
-    ga, mb, S = args.grad_accum, args.micro_batch, args.seq
+    cfg = bench_cfg(args, world)
+    mc = model_config(cfg)
+    pp, dp, tp = cfg["pp"], cfg["dp"], cfg["tp"]
+    ga, rows, S, mb = cfg["grad_accum_steps"], cfg["_rows"], cfg["seq_len"], cfg["micro_batch_size"]
+    nmb = cfg["num_microbatches"] if pp > 1 else 1
     try:
-        ctx = RCtx(OrderedDict([("pp", 1), ("dp", world), ("tp", 1)]))
+        ctx = RCtx(OrderedDict([("pp", pp), ("dp", dp), ("tp", tp)]))
         torch.manual_seed(1234)
+        layer_range = None
+        if pp > 1:
+            part = rpart(mc.num_hidden_layers, pp, strategy="uniform")[ctx.pp_rank]
+            layer_range = range(part[0], part[-1] + 1)
         with torch.device("meta"):
-            model = rbuild(cfg, ctx)
+            model = rbuild(mc, ctx, use_pp_aware=pp > 1, layer_range=layer_range)
         model = model.to_empty(device=device)
         for p in model.parameters():
             torch.nn.init.normal_(p, mean=0.0, std=0.02)
-        # the reference's own tests re-create rotary inv_freq after to_empty
+        # the reference's own tests re-create rotary inv_freq after to_empty (its random-init
+        # path leaves it uninitialised)
         rot = model.model.rotary_emb
-        dim = cfg.hidden_size // cfg.num_attention_heads
-        theta = (getattr(cfg, "rope_parameters", None) or {}).get("rope_theta", 10000.0)
+        dim = mc.hidden_size // mc.num_attention_heads
+        theta = (getattr(mc, "rope_parameters", None) or {}).get("rope_theta", cfg["rope_theta"])
         inv = 1.0 / (theta ** (torch.arange(0, dim, 2, dtype=torch.int64).to(
             device=device, dtype=torch.float) / dim))
         rot.inv_freq.copy_(inv)
         if hasattr(rot, "original_inv_freq"):
             rot.original_inv_freq.copy_(inv)
         model = model.bfloat16()
-        total = args.warmup + 2 * args.steps + 10
+        total = cfg["train_steps"]
         tc = RTC(master_dtype=torch.float32, grad_clip=None, train_steps=total, log_interval=10 ** 9,
-                 checkpoint_interval=10 ** 9, warmup_steps=2, min_lr_ratio=0.1)
+                 checkpoint_interval=10 ** 9, warmup_steps=2, min_lr_ratio=0.1,
+                 pipeline_config=RPC(num_microbatches=nmb, schedule=cfg["schedule"]))
         tc.grad_accum_steps = ga
-        strategy = rstrat(ctx, RZ(stage=3, wrap_policy=get_wrap_policy("llama_decoder_layer")))
+        wrap = get_wrap_policy("llama_decoder_layer") if cfg["zero_stage"] == 3 else None
+        strategy = rstrat(ctx, RZ(stage=cfg["zero_stage"], wrap_policy=wrap))
         mp = RMP(model=model, sharding_strategy=strategy, parallel_ctx=ctx, parallel_plan=rplan(),
                  config=tc, inner_optimizer_cls=torch.optim.AdamW,
                  inner_optimizer_kwargs={"lr": 3e-4, "betas": (0.9, 0.95), "eps": 1e-8},
                  compute_param_groups=rgroups(model, weight_decay=0.01))
-        rac(model, get_ac_policy("llama_decoder_layer"), use_reentrant=False, preserve_rng_state=False)
+        if cfg["ac_enabled"]:
+            rac(model, get_ac_policy("llama_decoder_layer"), use_reentrant=False, preserve_rng_state=False)
         sched = rlr(mp.inner, warmup_steps=2, total_steps=total, min_lr_ratio=0.1)
+        runner = None
+        if pp > 1:
+            stage = RStage(model, ctx, loss_scale=1.0 / (ga * nmb))
+            comm = RComm(ctx, seqlen=S, hidden_size=mc.hidden_size, dtype=torch.bfloat16)
+            runner = RRunner(stage, comm, schedule_name=cfg["schedule"], num_microbatches=nmb,
+                             recv_shape=(mb, S, mc.hidden_size), recv_dtype=torch.bfloat16)
         g = torch.Generator()
         g.manual_seed(7)
-        data = torch.randint(0, cfg.vocab_size, (ga * mb * world * (args.warmup + args.steps + 2), S), generator=g)
-        dl = RDL(dataset=data, parallel_ctx=ctx, micro_batch_size=mb, collator=rcoll, num_workers=2)
+        data = torch.randint(0, mc.vocab_size, (ga * rows * dp * (args.warmup + args.steps + 2), S), generator=g)
+        dl = RDL(dataset=data, parallel_ctx=ctx, micro_batch_size=rows, collator=rcoll, num_workers=2)
         gs = rsync(mp.groups, ctx, strategy)
         trainer = RTrainer(model=model, mp_manager=mp, scheduler=sched, dataloader=dl, grad_sync=gs,
-                           parallel_ctx=ctx, train_config=tc)
+                           parallel_ctx=ctx, train_config=tc, pp_runner=runner)
         mp.strategy.prepare_for_backward(mp.groups)
         dl.set_epoch(0)
         it = iter(dl)
@@ -401,20 +456,22 @@ def run_reference(args):
         emit({"impl": "reference", "unavailable": f"reference ran out of GPU memory on this config: {str(ex)[:160]}"})
         dist.destroy_process_group()
         return
-    tokens = ga * mb * S * world
+    tokens = ga * rows * S * dp
     value = tokens / (ms / 1e3)
     pk = peaks()
+    desc = describe(args, cfg)
+    if cfg.get("sequence_parallel"):
+        desc["parallelism"] = desc["parallelism"].replace("-sp", "") + " (reference: no sequence parallelism)"
     emit({"metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
           "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 2),
-          "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-          "data": "synthetic (uniform random token ids, random-init weights)",
-          "config": {"model": "Llama-3-8B" if not args.layers else f"Llama-3-8B-{args.layers}L(debug)",
-                     "global_batch": ga * mb * world, "seq_len": S, "parallelism": f"zero3-dp{world}",
-                     "activation_checkpointing": "full"},
-          "mfu": round(value * flops_per_token(cfg, S) / (world * pk["bf16_tflops"] * 1e12), 4),
+          "higher_is_better": True, "scaling": CONFIGS[args.config]["scaling"], "vs_baseline": None,
+          "dtype": "bf16", "data": "synthetic (uniform random token ids, random-init weights)",
+          "config": desc,
+          "mfu": round(value * flops_per_token(mc, S) / (world * pk["bf16_tflops"] * 1e12), 4),
           "loss_last": info["loss"] if info else None,
           "e2e": {"value": tokens / (wall / 1e3), "unit": "tokens/s", "ms_per_step": wall,
-                  "h2d_bytes_per_step": ga * mb * S * 8 * 2, "d2h_bytes_per_step": 4},
+                  "h2d_bytes_per_step": ga * rows * S * 8 * 2, "d2h_bytes_per_step": 4},
+          "peak_mem_gb": round(max_over_ranks(torch.cuda.max_memory_allocated(device) / 2 ** 30), 1),
           "impl": "reference", "clocks": clk.summary()})
     dist.barrier()
     dist.destroy_process_group()

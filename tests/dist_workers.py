@@ -316,8 +316,14 @@ def w_failure_modes(rank, world, tmpdir):
     # -- NaN abort
     nan_tr = _build_trainer(cfg, sd, ctx, 3, steps=2, mb=2, ga=1, seed_data=9, check_finite=True)
     with torch.no_grad():
-        emb = nan_tr.model.model.embed_tokens.weight
-        emb.fill_(float("nan"))
+        # under ZeRO-3 the embedding is sharded like every other parameter: its storage is
+        # this rank's slice of its cluster, gathered at the next forward
+        owner = [c for c in nan_tr.mp_manager.clusters
+                 if any(pg.name.endswith("embed_tokens.weight") for pg in c.param_groups)]
+        if owner:
+            owner[0].flat_param_shard.fill_(float("nan"))
+        else:
+            nan_tr.model.model.embed_tokens.weight.fill_(float("nan"))
     nan_tr.dataloader.set_epoch(0)
     try:
         nan_tr.train_step(iter(nan_tr.dataloader))
