@@ -164,9 +164,11 @@ void rs_adamw(const std::vector<int64_t>& src_ptrs, int64_t base, int64_t n, boo
   const int nsrc = static_cast<int>(src_ptrs.size());
   TORCH_CHECK(nsrc >= 1 && nsrc <= RSA_MAX_SRC, "rs_adamw: 1..8 sources");
   TORCH_CHECK(n % 8 == 0 && n >= 0, "rs_adamw: slice length must be a multiple of 8");
-  TORCH_CHECK(grad_shard.scalar_type() == at::kFloat && grad_shard.is_contiguous() &&
-              grad_shard.numel() >= n && aligned16(grad_shard.data_ptr()),
-              "rs_adamw: grad_shard must be fp32, contiguous, 16-byte aligned, >= n");
+  // grad_shard is read when accumulating and written when store_grad; otherwise it may be empty
+  if (accumulate || store_grad)
+    TORCH_CHECK(grad_shard.scalar_type() == at::kFloat && grad_shard.is_contiguous() &&
+                grad_shard.numel() >= n && aligned16(grad_shard.data_ptr()),
+                "rs_adamw: grad_shard must be fp32, contiguous, 16-byte aligned, >= n");
   RSAdamArgs a{};
   const int64_t es = src_f32 ? 4 : 2;
   for (int r = 0; r < nsrc; ++r) {
@@ -179,7 +181,7 @@ void rs_adamw(const std::vector<int64_t>& src_ptrs, int64_t base, int64_t n, boo
   a.n = n;
   a.scale = static_cast<float>(scale);
   a.accumulate = accumulate ? 1 : 0;
-  a.grad_shard = grad_shard.data_ptr<float>();
+  a.grad_shard = (accumulate || store_grad) ? grad_shard.data_ptr<float>() : nullptr;
   a.store_grad = store_grad ? 1 : 0;
   if (master.has_value() && master->defined() && master->numel() > 0) {
     TORCH_CHECK(m.has_value() && v.has_value() && p16.has_value() && segments.has_value(),

@@ -101,7 +101,10 @@ class ParamGroupCluster:
             if l.has_local_view:
                 self.param_views[pg.name] = self.master.narrow(0, l.local_offset, l.local_numel).detach().requires_grad_(True)
                 self.compute_views[pg.name] = self.flat_param_shard.narrow(0, l.local_offset, l.local_numel)
-        self.flat_grad_shard = torch.zeros(self.shard_size, dtype=torch.float32, device=self.device)
+        # dp > 1: allocated on first use -- the fused reduce-scatter + AdamW never needs it
+        self._flat_grad_shard: torch.Tensor | None = None
+        if self.direct:
+            self._flat_grad_shard = torch.zeros(self.shard_size, dtype=torch.float32, device=self.device)
         # dp > 1: the first reduce-scatter of a step overwrites instead of adding
         self._grad_fresh = not self.direct
         self._full_buffer: torch.Tensor | None = None
@@ -112,6 +115,13 @@ class ParamGroupCluster:
         self.updated_early = False
         self.opt_config = dict(param_groups[0].opt_config)
         self._take_over_param_groups()
+
+    @property
+    def flat_grad_shard(self) -> torch.Tensor:
+        """fp32 gradient of this rank's shard (allocated on first use)."""
+        if self._flat_grad_shard is None:
+            self._flat_grad_shard = torch.zeros(self.shard_size, dtype=torch.float32, device=self.device)
+        return self._flat_grad_shard
 
     # ------------------------------------------------------------------ construction
     def _initialize_flat_param_shard(self) -> torch.Tensor:
@@ -295,13 +305,20 @@ class ParamGroupCluster:
                 C.rs_adamw(srcs, base, self.shard_size, f32, scale, accumulate, self.flat_grad_shard,
                            True, None, None, None, None, None, 0.9, 0.999, 1e-8, 1)
             else:
-                C.rs_adamw(srcs, base, self.shard_size, f32, scale, accumulate, self.flat_grad_shard,
-                           True, self.master, upd["exp_avg"], upd["exp_avg_sq"], self.flat_param_shard,
+                # the fp32 gradient shard is only written when it exists already (direct mode,
+                # or an earlier reduction of this step): the update itself does not need it
+                keep = self._flat_grad_shard is not None
+                gs = self._flat_grad_shard if keep else self.master[:0]
+                C.rs_adamw(srcs, base, self.shard_size, f32, scale, accumulate and keep, gs,
+                           keep, self.master, upd["exp_avg"], upd["exp_avg_sq"], self.flat_param_shard,
                            upd["segments"], upd["beta1"], upd["beta2"], upd["eps"], upd["step"])
                 self.updated_early = True
 
     def populate_master_grad(self) -> None:
-        """Point the optimizer's views at the reduced fp32 gradient (no copy)."""
+        """Point the optimizer's views at the reduced fp32 gradient (no copy).  Nothing to do
+        when the fused reduce-scatter already applied this step's update."""
+        if self.updated_early:
+            return
         if self._grad_fresh:
             self.flat_grad_shard.zero_()
             self._grad_fresh = False
@@ -332,7 +349,7 @@ class ParamGroupCluster:
             "name": self.name,
             "flat_param_shard_bytes": self.shard_size * es,
             "master_bytes": self.master.numel() * self.master.element_size(),
-            "flat_grad_shard_bytes": self.flat_grad_shard.numel() * 4,
+            "flat_grad_shard_bytes": self._flat_grad_shard.numel() * 4 if self._flat_grad_shard is not None else 0,
             "full_buffer_bytes": (self.padded_size * es) if self._full_buffer is not None else 0,
         }
 

@@ -90,9 +90,11 @@ class ZeRO3Strategy:
         self.in_final_backward = False
 
     def make_master(self, compute: nn.Parameter, master_dtype: torch.dtype):
-        master = compute.detach().clone().to(master_dtype)
-        master.requires_grad_(True)
-        return master, None
+        # clusters build their own sharded fp32 masters; parameters that stay unsharded get
+        # theirs in make_clusters (a full fp32 copy of every parameter first would cost
+        # 4 bytes per parameter of transient memory, 70 GB per GPU on a 70B model at TP=4)
+        self._master_dtype = master_dtype
+        return None, None
 
     # ------------------------------------------------------------------ construction
     def make_clusters(self, model: nn.Module, groups: list, master_dtype):
@@ -190,10 +192,11 @@ class ZeRO3Strategy:
             # LM-head + loss), so the gathers hang off the root module's forward
             self._hook_handles.append(
                 model.register_forward_pre_hook(lambda mod, args: self._pre_forward_root()))
-        # unsharded free parameters (one rank, or sharding disabled) accumulate an fp32
-        # gradient in place, all-reduced at step time
+        # unsharded free parameters (one rank, or sharding disabled) get a full fp32 master and
+        # accumulate an fp32 gradient in place, all-reduced at step time
         for pg in groups:
             if pg.cluster is None and pg.compute.requires_grad:
+                pg.master = pg.compute.detach().clone().to(master_dtype).requires_grad_(True)
                 pg.compute.main_grad = torch.zeros(pg.compute.shape, dtype=torch.float32,
                                                    device=pg.compute.device)
         self.shards_written()

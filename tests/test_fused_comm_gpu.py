@@ -103,8 +103,8 @@ def test_scatter_epilogue_stores_rows_at_their_owner(world, Tl, N, K):
 
 
 @pytest.mark.parametrize("R,f32", [(1, True), (2, False), (4, True), (8, True), (8, False)])
-@pytest.mark.parametrize("accumulate", [False, True])
-def test_rs_adamw_matches_mean_and_torch_adamw(R, f32, accumulate):
+@pytest.mark.parametrize("accumulate,store", [(False, True), (True, True), (False, False)])
+def test_rs_adamw_matches_mean_and_torch_adamw(R, f32, accumulate, store):
     torch.manual_seed(3)
     C = native()
     n, shard_rank = 8192, 1 if R > 1 else 0
@@ -120,13 +120,17 @@ def test_rs_adamw_matches_mean_and_torch_adamw(R, f32, accumulate):
     segs = torch.tensor([[0, 5000, 1e-3, 0.1], [5000, 8000, 1e-3, 0.0]], dtype=torch.float64)
     step = 3
     ref_m, ref_v, ref_p = m.clone(), v.clone(), master.clone()
-    C.rs_adamw([b.data_ptr() for b in bufs], shard_rank * n, n, f32, 1.0 / R, accumulate, grad,
-               True, master, m, v, p16, segs, 0.9, 0.95, 1e-8, step)
+    gs = grad if (accumulate or store) else grad[:0]   # no gradient shard at all
+    C.rs_adamw([b.data_ptr() for b in bufs], shard_rank * n, n, f32, 1.0 / R, accumulate, gs,
+               store, master, m, v, p16, segs, 0.9, 0.95, 1e-8, step)
     torch.cuda.synchronize()
     g = sum(b[shard_rank * n:(shard_rank + 1) * n].float() for b in bufs) / R
     if accumulate:
         g = g + prev
-    assert torch.allclose(grad, g, atol=1e-5, rtol=1e-5)
+    if store:
+        assert torch.allclose(grad, g, atol=1e-5, rtol=1e-5)
+    else:
+        assert torch.equal(grad, prev)
     # torch.optim.AdamW on the same state, one segment at a time
     for (s, e, lr, wd) in segs.tolist():
         s, e = int(s), int(e)
