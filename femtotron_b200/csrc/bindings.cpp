@@ -54,8 +54,25 @@ void rs_adamw(const std::vector<int64_t>& src_ptrs, int64_t base, int64_t n, boo
               const c10::optional<torch::Tensor>& segments, double beta1, double beta2,
               double eps, int64_t step);
 void stream_write(int64_t addr, int64_t value);
-void sum_partials(const torch::Tensor& parts, const c10::optional<torch::Tensor>& resid,
-                  torch::Tensor& out);
+int64_t gate_reserved_sms();
+bool nvls_supported(int64_t device);
+int64_t nvls_round_size(int64_t device, int64_t world, int64_t nbytes);
+int64_t nvls_create(int64_t device, int64_t world, int64_t size);
+int64_t nvls_export_fd(int64_t id);
+int64_t nvls_import(int64_t device, int64_t world, int64_t size, int64_t fd);
+void nvls_add_device(int64_t id);
+std::vector<int64_t> nvls_bind_map(int64_t id);
+void nvls_close(int64_t id);
+void nvls_barrier(int64_t uc_base, int64_t mc_base, int64_t flag_off, int64_t target,
+                  torch::Tensor& err, int64_t code, int64_t timeout_ms);
+void nvls_reduce_slice(int64_t mc_base, int64_t nbytes, int64_t rank, int64_t world, bool f32,
+                       double scale);
+void ag_pull(const std::vector<int64_t>& src_ptrs, const std::vector<int64_t>& ready_ptrs,
+             torch::Tensor& dst, int64_t chunk_bytes, int64_t chunk_count_ptr, int64_t me,
+             int64_t epoch, int64_t ctas, torch::Tensor& err, int64_t timeout_ms);
+void rs_pull(const std::vector<int64_t>& src_ptrs, const std::vector<int64_t>& part_ptrs,
+             const c10::optional<torch::Tensor>& resid, torch::Tensor& out, int64_t nelem,
+             int64_t epoch, torch::Tensor& err, int64_t timeout_ms);
 void flash_fwd(const torch::Tensor& qkv, torch::Tensor& o, torch::Tensor& lse, int64_t B, int64_t S,
                int64_t nq, int64_t nkv, int64_t D, torch::Tensor& err);
 void flash_fwd_variant(const torch::Tensor& qkv, torch::Tensor& o, torch::Tensor& lse, int64_t B,
@@ -91,7 +108,19 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("wait_flags_geq", &ft::wait_flags_geq, "bounded wait for peer flags (one warp)");
   m.def("rs_adamw", &ft::rs_adamw, "ZeRO reduce-scatter + fp32 cast/scale + sharded AdamW");
   m.def("stream_write", &ft::stream_write);
-  m.def("sum_partials", &ft::sum_partials);
+  m.def("nvls_supported", &ft::nvls_supported);
+  m.def("nvls_round_size", &ft::nvls_round_size);
+  m.def("nvls_create", &ft::nvls_create);
+  m.def("nvls_export_fd", &ft::nvls_export_fd);
+  m.def("nvls_import", &ft::nvls_import);
+  m.def("nvls_add_device", &ft::nvls_add_device);
+  m.def("nvls_bind_map", &ft::nvls_bind_map);
+  m.def("nvls_close", &ft::nvls_close);
+  m.def("nvls_barrier", &ft::nvls_barrier, "NVLS barrier: multimem.red + bounded wait");
+  m.def("nvls_reduce_slice", &ft::nvls_reduce_slice, "in-switch reduction of this rank's slice (multimem)");
+  m.def("gate_reserved_sms", &ft::gate_reserved_sms, "SMs a gated GEMM leaves to the pull kernel");
+  m.def("ag_pull", &ft::ag_pull, "tensor-parallel all-gather: SM-driven peer pulls + chunk counters");
+  m.def("rs_pull", &ft::rs_pull, "tensor-parallel reduce-scatter: owner pulls and sums peer partials");
   m.def("flash_fwd", &ft::flash_fwd);
   m.def("flash_fwd_variant", &ft::flash_fwd_variant);
   m.def("flash_bwd", &ft::flash_bwd);

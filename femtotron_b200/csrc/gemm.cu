@@ -659,11 +659,11 @@ static int num_sms() {
   return n;
 }
 
-// A gated GEMM (fused all-gather) waits for chunks that copy engines bring in after a
-// bounded wait kernel on the copy stream has seen the peers' ready flags.  A persistent grid
-// over every SM could leave that one-warp kernel no SM to run on while the GEMM waits for
-// it, so gated launches leave a few SMs free.
-constexpr int GATE_RESERVED_SMS = 4;
+// A gated GEMM (fused all-gather) waits for chunks that the pull kernel (tp_comm.cu) brings
+// in from the peers on a side stream, one CTA per SM.  A persistent grid over every SM could
+// leave that kernel no SM to run on while the GEMM waits for it, so gated launches leave
+// GATE_RESERVED_SMS SMs free, and the pull kernel runs exactly that many CTAs.
+constexpr int GATE_RESERVED_SMS = 16;
 
 static int usable_sms(const Params& p) {
   return p.gate_op != 0 ? std::max(2, num_sms() - GATE_RESERVED_SMS) : num_sms();
@@ -717,6 +717,8 @@ static int choose_bn(int M, int N, bool swiglu) {
 }
 
 }  // namespace gemm
+
+int64_t gate_reserved_sms() { return gemm::GATE_RESERVED_SMS; }
 
 struct GateScatter {
   int64_t gate_flags = 0;

@@ -1,41 +1,44 @@
 """Fused tensor-parallel communication for sequence parallelism on NVLink (one process per
-GPU): all-gather -> GEMM and GEMM -> reduce-scatter without SM-driven collectives.
+GPU): all-gather -> GEMM and GEMM -> reduce-scatter driven by this library's kernels.
 
 All-gather (AG) of a token-sharded activation x_local [Tl, H] into x_full [T = tp*Tl, H]:
-  1. the rank stages x_local in its symmetric slot and writes epoch e into every peer's
-     READY[me] flag (stream memory op, system-scope fence first);
-  2. on a copy stream a one-warp kernel waits (bounded) until every READY[r] >= e, then the
-     copy engines pull each rank's slot (own first) into the local x_full, each pull followed
-     by a stream write CHUNK[r] = e; afterwards it writes DONE[me] = e into every peer (the
-     slot may be reused);
-  3. the consuming GEMM is launched on the compute stream at once: its TMA producer waits
-     (bounded, in-kernel) on CHUNK[r] for the rows of each tile, so MMAs on local rows start
-     while peer rows are still in flight, and each remote row crosses NVLink exactly once.
+  1. after a bounded wait for every peer's DONE flag of two epochs ago (they finished reading
+     this slot), the rank stages x_local in its symmetric slot and writes epoch e into every
+     peer's READY[me] flag (stream memory write, system-scope fence first);
+  2. on a side stream the pull kernel (``ag_pull``, one CTA on each of the SMs the gated GEMM
+     leaves free) visits the ranks in ring order starting with itself, waits (bounded) for the
+     owner's READY flag, copies the owner's chunk over NVLink into x_full with wide loads and
+     bumps the chunk's local counter; afterwards the stream writes DONE[me] = e into every
+     peer;
+  3. the consuming GEMM runs on the compute stream at once: its TMA producer waits (bounded)
+     until the counter of every chunk its tile rows touch reaches e x CTAs, so MMAs on the
+     local chunk start immediately and peer rows are consumed as they land; every remote row
+     crosses NVLink exactly once.
 Reduce-scatter (RS) of a row-parallel GEMM's partial output over tokens:
-  1. the GEMM epilogue stores every output row straight into the receive slot of the rank
-     that owns that token (P2P stores over NVLink), then PART[me] = e is written to every
-     owner after the GEMM;
-  2. the owner's compute stream waits (bounded kernel) for PART[r] >= e from all ranks, sums
-     the tp partials of its rows in fp32 and adds the residual in one kernel, then writes
-     CONS[me] = e into every peer so the slot can be rewritten.
+  1. after a bounded wait for every peer's CONS flag of two epochs ago, the GEMM stores its
+     full partial [T, N] into this rank's symmetric slot (local stores) and the stream writes
+     PART[me] = e into every peer;
+  2. the owner of rows [me*Tl, (me+1)*Tl) runs ``rs_pull``: it waits (bounded) for every
+     PART flag, sums those rows of every peer's slot in fp32 over NVLink, adds the residual,
+     writes bf16, and then the stream writes CONS[me] = e into every peer.
 Slots are double-buffered per direction; epochs increase monotonically and every rank makes
 the same sequence of calls, so stale flags are never mistaken for fresh ones.
 
-Every wait is a kernel with a time limit (``wait_flags_geq``; FT_COMM_TIMEOUT_MS, default
-30 s): a peer that never publishes makes the waiting rank record an error code (200 + flag
-kind offset + peer) and continue, and the host raises KernelTimeoutError at its next
-``check_kernel_errors``.  The gated GEMM leaves a few SMs free so that the copy stream's wait
-kernel can always run while the GEMM waits for the copies it releases.
+Every wait is a kernel with a time limit (FT_COMM_TIMEOUT_MS, default 30 s): a peer that never
+publishes makes the waiting rank record an error code (200 + flag-kind offset + peer) and
+continue, and the host raises KernelTimeoutError at its next ``check_kernel_errors``.  The
+gated GEMM leaves ``gate_reserved_sms()`` SMs free, and the pull kernel runs exactly that many
+CTAs, so the two always run side by side.
 """
 from __future__ import annotations
+
+import os
 
 import torch
 import torch.distributed as dist
 
 from femtotron_b200.ops.ext import error_flag, native
 from femtotron_b200.parallel.symm import SymmetricAllocator, SymmetricHeap
-
-import os
 
 KINDS = ("READY", "DONE", "PART", "CONS", "CHUNK")
 NSLOTS = 2
@@ -53,11 +56,12 @@ class TPFusedComm:
         self.slot_elems = rows_local * cols
         sb = self.slot_elems * 2
         a = SymmetricAllocator()
-        self.off_ag = a.reserve("ag", NSLOTS * sb)
-        self.off_rs = a.reserve("rs", NSLOTS * world * sb)
+        self.off_ag = a.reserve("ag", NSLOTS * sb)              # this rank's staged shard
+        self.off_rs = a.reserve("rs", NSLOTS * world * sb)      # this rank's full partial
         self.off_flags = a.reserve("flags", len(KINDS) * 64 * 4)
         self.heap = SymmetricHeap(group, None, a.size, device)
         self.cs = torch.cuda.Stream(device=device)
+        self.ctas = int(native().gate_reserved_sms())
         self.ag_epoch = 0
         self.rs_epoch = 0
 
@@ -76,15 +80,20 @@ class TPFusedComm:
         native().wait_flags_geq([self.local_flag(kind, r) for r in range(self.world)], epoch,
                                 error_flag(self.device), COMM_TIMEOUT_MS, WAIT_CODES[kind])
 
+    def publish(self, kind: str, epoch: int) -> None:
+        """Write epoch into every rank's `kind`[me] flag once the current stream's work is done."""
+        C = native()
+        for r in range(self.world):
+            C.stream_write(self.peer_flag(r, kind, self.rank), epoch)
+
     def fits(self, rows_local: int, cols: int) -> bool:
         return rows_local * cols <= self.slot_elems
 
     # ------------------------------------------------------------------ all-gather
     def all_gather(self, x_local: torch.Tensor):
         """Start gathering x_local [Tl, H] (bf16, contiguous); returns (x_full, epoch).  The
-        rows of rank r become valid when CHUNK[r] >= epoch (gate the consuming GEMM on it);
-        work queued on the current stream after this call also sees x_full complete."""
-        C = native()
+        rows of rank r are valid once CHUNK[r] >= epoch x CTAs (gate the consuming GEMM on
+        it); work queued on the current stream after ``after_gated`` sees x_full complete."""
         Tl, H = x_local.shape
         e = self.ag_epoch = self.ag_epoch + 1
         s = e % NSLOTS
@@ -93,60 +102,55 @@ class TPFusedComm:
             self.wait_all("DONE", e - NSLOTS)
         slot_off = self.off_ag + s * self.slot_elems * 2
         self.heap.view(slot_off, Tl * H, torch.bfloat16).copy_(x_local.reshape(-1))
-        for r in range(self.world):
-            C.stream_write(self.peer_flag(r, "READY", self.rank), e)
+        self.publish("READY", e)
         full = torch.empty(self.world * Tl, H, dtype=torch.bfloat16, device=self.device)
-        nb = Tl * H * 2
         self.cs.wait_stream(cur)
         with torch.cuda.stream(self.cs):
-            self.wait_all("READY", e)
-            for k in range(self.world):
-                r = (self.rank + k) % self.world
-                C.copy_from_ptrs([full.data_ptr() + r * nb], [self.heap.peer_ptr(r, slot_off)], [nb])
-                C.stream_write(self.local_flag("CHUNK", r), e)
-            for r in range(self.world):
-                C.stream_write(self.peer_flag(r, "DONE", self.rank), e)
+            native().ag_pull([self.heap.peer_ptr(r, slot_off) for r in range(self.world)],
+                             [self.local_flag("READY", r) for r in range(self.world)],
+                             full, Tl * H * 2, self.local_flag("CHUNK", 0), self.rank, e,
+                             self.ctas, error_flag(self.device), COMM_TIMEOUT_MS)
+            self.publish("DONE", e)
         full.record_stream(self.cs)
         return full, e
 
     def gate(self, epoch: int, rows_local: int, cols: int) -> dict:
-        return dict(gate_flags=self.local_flag("CHUNK", 0), gate_op=1, gate_epoch=epoch, gate_off=0,
-                    gate_row_elems=cols, gate_chunk_elems=rows_local * cols)
+        return dict(gate_flags=self.local_flag("CHUNK", 0), gate_op=1, gate_epoch=epoch * self.ctas,
+                    gate_off=0, gate_row_elems=cols, gate_chunk_elems=rows_local * cols)
 
     def after_gated(self) -> None:
-        """Order later work on the current stream after the copy engines' pulls."""
+        """Order later work on the current stream after the pull kernel."""
         torch.cuda.current_stream(self.device).wait_stream(self.cs)
 
     # ------------------------------------------------------------------ reduce-scatter
     def rs_begin(self, rows_local: int, cols: int):
-        """Returns (epoch, scatter pointers) for a GEMM whose row r goes to owner r // Tl."""
-        C = native()
+        """Returns (epoch, partial): the [T, cols] buffer the row-parallel GEMM stores into."""
         e = self.rs_epoch = self.rs_epoch + 1
         s = e % NSLOTS
         if e > NSLOTS:
             self.wait_all("CONS", e - NSLOTS)
-        sb = self.slot_elems * 2
-        ptrs = [self.heap.peer_ptr(r, self.off_rs + (s * self.world + self.rank) * sb)
-                for r in range(self.world)]
-        return e, ptrs
+        T = self.world * rows_local
+        off = self.off_rs + s * self.world * self.slot_elems * 2
+        return e, self.heap.view(off, T * cols, torch.bfloat16).view(T, cols)
 
-    def rs_finish(self, e: int, rows_local: int, cols: int, residual: torch.Tensor | None):
-        C = native()
+    def rs_publish(self, e: int) -> None:
+        """Tell every peer that this rank's partial of epoch e is complete."""
+        self.publish("PART", e)
+
+    def rs_finish(self, e: int, rows_local: int, cols: int, residual: torch.Tensor | None,
+                  published: bool = False):
+        """This rank's rows of the sum over ranks of the partials (+ residual)."""
+        if not published:
+            self.rs_publish(e)
         s = e % NSLOTS
-        for r in range(self.world):
-            C.stream_write(self.peer_flag(r, "PART", self.rank), e)
-        self.wait_all("PART", e)
-        sb = self.slot_elems * 2
-        base = self.off_rs + s * self.world * sb
+        n = rows_local * cols
+        base = self.off_rs + s * self.world * self.slot_elems * 2 + self.rank * n * 2
         out = torch.empty(rows_local, cols, dtype=torch.bfloat16, device=self.device)
-        if self.slot_elems == rows_local * cols:
-            parts = self.heap.view(base, self.world * rows_local * cols, torch.bfloat16).view(self.world, -1)
-        else:  # slots are larger than this call's payload: gather the used prefixes
-            parts = torch.stack([self.heap.view(base + r * sb, rows_local * cols, torch.bfloat16)
-                                 for r in range(self.world)])
-        C.sum_partials(parts, residual.reshape(-1) if residual is not None else None, out)
-        for r in range(self.world):
-            C.stream_write(self.peer_flag(r, "CONS", self.rank), e)
+        native().rs_pull([self.heap.peer_ptr(r, base) for r in range(self.world)],
+                         [self.local_flag("PART", r) for r in range(self.world)],
+                         residual.reshape(-1) if residual is not None else None, out, n, e,
+                         error_flag(self.device), COMM_TIMEOUT_MS)
+        self.publish("CONS", e)
         return out
 
     def close(self):
@@ -190,17 +194,15 @@ from torch.autograd import Function  # noqa: E402
 
 from femtotron_b200.ops import kernels as K  # noqa: E402
 from femtotron_b200.ops.functional import cat_rows_view, write_weight_grad  # noqa: E402
-from femtotron_b200.ops.matmul import linear_wgrad  # noqa: E402
-
-
-def _scatter_dummy(M, N, device):
-    return torch.empty(1, dtype=torch.bfloat16, device=device).expand(M, N)
+from femtotron_b200.ops.matmul import gemm, linear_wgrad  # noqa: E402
 
 
 def _dgrad_rs(comm, d, W, Tl, H):
-    """dx_local [Tl, H] = reduce-scatter over tokens of d [T, N] @ W [N, H] (fused)."""
-    e, ptrs = comm.rs_begin(Tl, H)
-    fused_gemm(d, W, _scatter_dummy(d.shape[0], H, d.device), b_mn=True, scatter=(ptrs, Tl))
+    """Start dx_local [Tl, H] = reduce-scatter over tokens of d [T, N] @ W [N, H]: the dgrad
+    GEMM stores the partial into the symmetric slot and the peers are told at once."""
+    e, part = comm.rs_begin(Tl, H)
+    gemm(d, W, part, b_mn=True)
+    comm.rs_publish(e)
     return e
 
 
@@ -251,14 +253,14 @@ class SPColumnFn(Function):
         W = cat_rows_view(ws)
         e = _dgrad_rs(comm, d, W, ctx.Tl, ctx.H)
         write_weight_grad(ctx.params, lambda dst, acc: linear_wgrad(d, full, dst, acc))
-        dx = comm.rs_finish(e, ctx.Tl, ctx.H, None)
+        dx = comm.rs_finish(e, ctx.Tl, ctx.H, None, published=True)
         ctx.params = None
         return (dx.view(ctx.xshape), None, None, None) + (None,) * len(ws)
 
 
 class SPRowFn(Function):
-    """Row-parallel projection under sequence parallelism: GEMM whose epilogue scatters rows
-    to their token owners, owner-side sum of the partials plus the residual (fused GEMM ->
+    """Row-parallel projection under sequence parallelism: GEMM into the symmetric partial
+    slot, owner-side pull and sum of the partials plus the residual (fused GEMM ->
     reduce-scatter); backward gathers the output gradient with the fused all-gather."""
 
     @staticmethod
@@ -267,8 +269,8 @@ class SPRowFn(Function):
         W = cat_rows_view(weights)
         T, N = h2.shape[0], W.shape[0]
         Tl = T // comm.world
-        e, ptrs = comm.rs_begin(Tl, N)
-        fused_gemm(h2, W, _scatter_dummy(T, N, h2.device), scatter=(ptrs, Tl))
+        e, part = comm.rs_begin(Tl, N)
+        gemm(h2, W, part)
         res = residual.reshape(-1, N).contiguous() if residual is not None else None
         out = comm.rs_finish(e, Tl, N, res)
         ctx.save_for_backward(h2, *[w.detach() for w in weights])

@@ -22,23 +22,33 @@ With a symmetric heap (CUDA, dp > 1) the packed parameter shard and the unsharde
 buffer live in IPC-shared memory:
   * all-gather: copy-engine pulls of every peer's shard (no SM, no flag: a shard only changes
     in the optimizer step, and every step ends with a device-side barrier);
-  * reduce-scatter: a one-element NCCL all-reduce on the reduce stream orders the ranks
-    (every rank has finished this unit's backward), then one kernel (``rs_adamw``) reads this
-    rank's slice of every peer's buffer over NVLink, averages in fp32 and writes the fp32
-    gradient shard -- and, when the optimizer allows it, applies AdamW to the shard and writes
-    the bf16 parameter shard in the same pass.  No stream or kernel ever waits on a flag
-    written by a peer, so the path cannot hang on a peer that fell behind: NCCL's own
-    collective (with the process group's timeout) is the only cross-rank wait.
+  * reduce-scatter: after the unit's last backward of the step, the compute stream writes the
+    unit's epoch into every peer's flag slot for this rank (a stream memory write, no SM);
+    on the reduce stream a one-warp kernel waits, with a time limit, until every peer's flag
+    for the unit reached the epoch, then one kernel (``rs_adamw``) reads this rank's slice of
+    every peer's buffer over NVLink, averages in fp32 and writes the fp32 gradient shard --
+    and, when the optimizer allows it, applies AdamW to the shard and writes the bf16
+    parameter shard in the same pass.  A peer that falls behind makes the wait give up with
+    an error code (KernelTimeoutError on the host) instead of hanging.  NCCL is not called
+    from the backward at all: its only use per step is the barrier at the end of the step,
+    from the training loop's thread, which also tells every rank that its peers finished
+    reading its gradient buffers.
 The reference does both with NCCL collectives (femtotron/sharding/param_group_cluster.py:
 248-252, :321-324) and the update as separate passes (mixed_precision_manager.py:318-331).
 """
 from __future__ import annotations
+
+import os
 
 import torch
 import torch.distributed as dist
 from torch import nn
 
 from .cluster_sharding_spec import compute_cluster_layout
+
+# bound of the wait for the peers' gradient flags (a peer that late has failed)
+RS_TIMEOUT_MS = int(os.environ.get("FT_COMM_TIMEOUT_MS", "30000"))
+RS_WAIT_CODE = 120   # + index of the first peer whose flag is missing
 
 
 class ParamGroupCluster:
@@ -48,7 +58,7 @@ class ParamGroupCluster:
 
     def __init__(self, name: str, module: nn.Module | None, param_groups: list, dp_group,
                  master_dtype: torch.dtype, comm_stream: torch.cuda.Stream | None = None,
-                 symm=None, grad_offset: int | None = None):
+                 symm=None, grad_offset: int | None = None, flag_offset: int | None = None):
         if not param_groups:
             raise ValueError(f"cluster {name}: empty param_groups")
         for pg in param_groups:
@@ -77,8 +87,11 @@ class ParamGroupCluster:
         # (SymmetricHeap, byte offset): flat_param_shard lives in symmetric memory and the
         # all-gather is a set of copy-engine pulls of every peer's shard (no SMs used)
         self.symm = symm
-        # byte offset of the unit's unsharded gradient buffer in the same heap
+        # byte offsets of the unit's unsharded gradient buffer and of its flag array (one
+        # int32 per rank: the last epoch for which that rank's buffer is complete) in the heap
         self.grad_offset = grad_offset if symm is not None else None
+        self.flag_offset = flag_offset if symm is not None else None
+        self._rs_epoch = 0
         # stream of the reduce-scatter (and of the fused update); set by the strategy
         self.rs_stream = None
         # dtype of the unsharded gradient buffer the backward accumulates into (dp > 1);
@@ -90,8 +103,6 @@ class ParamGroupCluster:
         # optional callable(cluster) -> dict of fused-AdamW arguments for this step's update of
         # the shard, or None; installed by the mixed-precision manager
         self.early_update = None
-        # one-element tensor of the ordering collective before each reduce-scatter
-        self.order_token: torch.Tensor | None = None
 
         self.flat_param_shard = self._initialize_flat_param_shard()
         self.master = self.flat_param_shard.to(master_dtype)
@@ -286,18 +297,26 @@ class ParamGroupCluster:
         C = native()
         cur = torch.cuda.current_stream(self.device)
         st = self.rs_stream or self.comm_stream or cur
-        st.wait_stream(cur)
         upd = self.early_update(self) if self.early_update is not None else None
         if self.direct and upd is None:
             return      # the gradient is already complete in flat_grad_shard
+        if not self.direct:
+            # publish: this rank's buffer of the unit is complete for epoch ep (written into
+            # every peer's flag array once the compute stream's backward kernels are done)
+            self._rs_epoch += 1
+            ep = self._rs_epoch
+            heap = self.symm[0]
+            for r in range(self.dp_size):
+                C.stream_write(heap.peer_ptr(r, self.flag_offset) + 4 * self.dp_rank, ep)
+        st.wait_stream(cur)
         with torch.cuda.stream(st):
             if self.direct:
                 srcs, base, f32, scale = [self.flat_grad_shard.data_ptr()], 0, True, 1.0
             else:
-                # every rank has finished writing this unit's gradient buffer once this
-                # collective completes (NCCL orders it with the rank's earlier work)
-                dist.all_reduce(self.order_token, op=dist.ReduceOp.MAX, group=self.dp_group)
-                heap = self.symm[0]
+                from femtotron_b200.ops.ext import error_flag
+                local = heap.peer_ptr(self.dp_rank, self.flag_offset)
+                C.wait_flags_geq([local + 4 * r for r in range(self.dp_size)], ep,
+                                 error_flag(self.device), RS_TIMEOUT_MS, RS_WAIT_CODE)
                 srcs = [heap.peer_ptr(r, self.grad_offset) for r in range(self.dp_size)]
                 base, f32 = self.dp_rank * self.shard_size, self.grad_dtype == torch.float32
                 scale = 1.0 / self.dp_size

@@ -162,18 +162,18 @@ class ZeRO3Strategy:
             for i, (u, pgs) in enumerate(unit_pgs + free_pgs):
                 shard = ParamGroupCluster.shard_numel(pgs, self.dp_size, al)
                 offsets.append(alloc.reserve(f"unit{i}", shard * es))
-                grad_offsets.append(alloc.reserve(f"grad{i}", shard * self.dp_size * ges))
+                grad_offsets.append((alloc.reserve(f"grad{i}", shard * self.dp_size * ges),
+                                     alloc.reserve(f"flags{i}", 4 * self.dp_size)))
             self.heap = SymmetricHeap(self.dp_group, None, alloc.size, dev)
             self._barrier_t = torch.zeros(1, device=dev)
-        token = torch.zeros(1, dtype=torch.int32, device=dev) if cuda else None
         for i, (u, pgs) in enumerate(unit_pgs + free_pgs):
             c = ParamGroupCluster(names.get(u, type(u).__name__) or "<root>", u, pgs, self.dp_group,
                                   master_dtype, comm_stream=self.comm_stream,
                                   symm=(self.heap, offsets[i]) if use_symm else None,
-                                  grad_offset=grad_offsets[i] if use_symm else None)
+                                  grad_offset=grad_offsets[i][0] if use_symm else None,
+                                  flag_offset=grad_offsets[i][1] if use_symm else None)
             c.grad_dtype = grad_dtype
             c.rs_stream = self.rs_stream
-            c.order_token = token
             (self.clusters if i < len(unit_pgs) else self.free_clusters).append(c)
         self.keep_in_step = self._decide_keep(dev)
         for i, c in enumerate(self.clusters):

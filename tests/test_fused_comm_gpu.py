@@ -2,8 +2,10 @@
 
   * the GEMM operand gate of the fused all-gather -> GEMM (A rows and B rows), with the
     gated rows written and their flags released by another stream about 10 ms later;
-  * the scatter epilogue of the fused GEMM -> reduce-scatter (rows stored into their owner's
-    buffer);
+  * the scatter epilogue of the GEMM (rows stored into their owner's buffer);
+  * the pull kernels of the tensor-parallel collectives: ``ag_pull`` (peer chunks gathered in
+    ring order, per-chunk counters that a gated GEMM consumes while the pull runs) and
+    ``rs_pull`` (an owner sums its rows of every rank's partial, plus the residual);
   * the fused ZeRO reduce-scatter + fp32 cast/scale + AdamW kernel (``rs_adamw``) against
     the mean of the sources and ``torch.optim.AdamW``;
   * bounded waits: a flag that nothing sets ends the wait with an error code after its time
@@ -182,4 +184,67 @@ def test_host_wait_is_bounded():
         wait_event_bounded(ev, 0.1, "test")
     torch.cuda.synchronize()
     with pytest.raises(KernelTimeoutError, match="code 300"):
+        check_kernel_errors(dev)
+
+
+def test_ag_pull_gathers_every_chunk_and_feeds_the_gated_gemm():
+    """The tensor-parallel all-gather pull kernel with four emulated ranks: the peers' staged
+    chunks (local tensors) land in ring order in the gathered buffer, each chunk counter
+    reaches epoch x CTAs, and a GEMM gated on those counters, launched while the peers'
+    READY flags are still unset, computes on the gathered rows."""
+    C = native()
+    dev = torch.device(DEV, 0)
+    world, me, Tl, H, N, e = 4, 1, 512, 640, 768, 3
+    ctas = int(C.gate_reserved_sms())
+    torch.manual_seed(4)
+    chunks = [torch.randn(Tl, H, device=dev).to(torch.bfloat16) for _ in range(world)]
+    w = torch.randn(N, H, device=dev).to(torch.bfloat16)
+    ready = torch.zeros(world, dtype=torch.int32, device=dev)
+    # every epoch adds one count per CTA: after epochs 1..e-1 a counter holds (e-1) x CTAs
+    count = torch.full((world,), (e - 1) * ctas, dtype=torch.int32, device=dev)
+    full = torch.zeros(world * Tl, H, device=dev, dtype=torch.bfloat16)
+    out = torch.empty(world * Tl, N, device=dev, dtype=torch.bfloat16)
+    side, rel = torch.cuda.Stream(), torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    rel.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(rel):            # the peers publish about 10 ms later
+        torch.cuda._sleep(20_000_000)
+        for r in range(world):
+            C.stream_write(ready.data_ptr() + 4 * r, e)
+    with torch.cuda.stream(side):
+        C.ag_pull([c.data_ptr() for c in chunks], [ready.data_ptr() + 4 * r for r in range(world)],
+                  full, Tl * H * 2, count.data_ptr(), me, e, ctas, error_flag(dev), 5000)
+    gate = dict(gate_flags=count.data_ptr(), gate_op=1, gate_epoch=e * ctas, gate_off=0,
+                gate_row_elems=H, gate_chunk_elems=Tl * H)
+    fused_gemm(full, w, out, gate=gate)
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.current_stream().wait_stream(rel)
+    torch.cuda.synchronize()
+    want = torch.cat(chunks)
+    assert torch.equal(full, want)
+    assert count.tolist() == [e * ctas] * world
+    assert rel_err(out, want.float() @ w.float().t()) < 1e-2
+
+
+def test_rs_pull_sums_every_rank_partial_of_its_rows():
+    C = native()
+    dev = torch.device(DEV, 0)
+    world, me, Tl, N, e = 4, 2, 256, 1024, 5
+    torch.manual_seed(5)
+    parts = [torch.randn(world * Tl, N, device=dev).to(torch.bfloat16) for _ in range(world)]
+    resid = torch.randn(Tl, N, device=dev).to(torch.bfloat16)
+    flags = torch.full((world,), e, dtype=torch.int32, device=dev)
+    out = torch.empty(Tl, N, device=dev, dtype=torch.bfloat16)
+    off = me * Tl * N * 2
+    C.rs_pull([p.data_ptr() + off for p in parts], [flags.data_ptr() + 4 * r for r in range(world)],
+              resid.reshape(-1), out, Tl * N, e, error_flag(dev), 2000)
+    torch.cuda.synchronize()
+    want = sum(p[me * Tl:(me + 1) * Tl].float() for p in parts) + resid.float()
+    assert rel_err(out, want) < 5e-3
+    # a peer that never publishes: the reduction gives up with code 240 + peer
+    flags[3] = e - 1
+    C.rs_pull([p.data_ptr() + off for p in parts], [flags.data_ptr() + 4 * r for r in range(world)],
+              None, out, Tl * N, e, error_flag(dev), 200)
+    torch.cuda.synchronize()
+    with pytest.raises(KernelTimeoutError, match="code 243"):
         check_kernel_errors(dev)

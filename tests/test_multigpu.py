@@ -30,3 +30,19 @@ def test_zero3_and_tp_sp_on_two_gpus():
     assert r["z0"][-1] < r["z0"][0]
     assert abs(r["tp1"] - r["tp2_sp"]) < 2e-2, r
     assert r["grad_norm_rel_err"] < 5e-2, r
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                    reason="needs 2 GPUs")
+def test_nvls_all_reduce_matches_nccl():
+    """The in-switch (NVLS multimem) all-reduce against NCCL's on 2 GPUs."""
+    from dist_helpers import free_port
+    cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run",
+           "--nproc-per-node", "2", "--master-addr", "127.0.0.1", "--master-port", str(free_port()),
+           os.path.join(ROOT, "tests", "mgpu", "nvls_check.py")]
+    out = subprocess.run(cmd, capture_output=True, text=True, timeout=360)
+    assert out.returncode == 0, out.stdout[-3000:] + out.stderr[-3000:]
+    line = [l for l in out.stdout.splitlines() if l.startswith("RESULT ")][-1]
+    r = json.loads(line[len("RESULT "):])
+    assert r["worst_err_over_tol"] < 1.0, r
+    assert r["packed_ok"], r
