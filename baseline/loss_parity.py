@@ -76,6 +76,9 @@ def ours(cfg, sd, batches, args, device):
     sched = create_lr_schedule(mp.inner, 10, args.steps, 0.1)
     tr = Trainer(m, mp, sched, None, create_grad_synchronizer(mp.groups, ctx, st), ctx, tc)
     out = [tr.train_step(iter([{"input_ids": x, "labels": x}]))["loss"] for x in batches]
+    if device.type == "cuda":
+        from femtotron_b200.ops.ext import check_kernel_errors
+        check_kernel_errors(device)      # a bounded wait that gave up fails the comparison
     mp.cleanup()
     return out
 
@@ -111,7 +114,8 @@ def reference(cfg, sd, batches, args, device):
         # the reference's own tests recompute RoPE inv_freq after to_empty
         rot = ref.model.rotary_emb
         d = cfg.hidden_size // cfg.num_attention_heads
-        inv = 1.0 / (cfg.rope_theta ** (torch.arange(0, d, 2, dtype=torch.float32, device=device) / d))
+        theta = (getattr(cfg, "rope_parameters", None) or {}).get("rope_theta", 500000.0)
+        inv = 1.0 / (theta ** (torch.arange(0, d, 2, dtype=torch.float32, device=device) / d))
         rot.inv_freq.copy_(inv)
         if hasattr(rot, "original_inv_freq"):
             rot.original_inv_freq.copy_(inv)
@@ -152,7 +156,7 @@ def main() -> None:
     args = ap.parse_args()
     from transformers import LlamaConfig
     from femtotron_b200.utils.dist import init_distributed
-    rank, world, local = init_distributed("nccl", timeout_s=300)
+    rank, world, local = init_distributed("nccl", timeout_s=int(os.environ.get("FT_PG_TIMEOUT", "300")))
     device = torch.device("cuda", local)
     cfg = LlamaConfig(hidden_size=4096, intermediate_size=14336, num_attention_heads=32,
                       num_key_value_heads=8, num_hidden_layers=args.layers, vocab_size=128256,
