@@ -40,6 +40,45 @@ def nvls_available(device: torch.device) -> bool:
         return False
 
 
+def share_fd(group, fd: int | None, timeout_s: float = 120.0) -> int | None:
+    """Give rank 0's open file descriptor `fd` to every other rank of `group` (one node): rank 0
+    listens on an abstract Unix socket whose name the group broadcasts, and sends the
+    descriptor to each peer that connects (SCM_RIGHTS via ``socket.send_fds``).  Rank 0 passes
+    its descriptor and gets None back (it keeps its own); the others pass None and get their
+    own duplicate, which they close when done."""
+    rank, world = dist.get_rank(group), dist.get_world_size(group)
+    name = [None]
+    srv = None
+    if rank == 0:
+        if fd is None:
+            raise ValueError("share_fd: rank 0 must pass the descriptor")
+        name = ["\0femtotron_fd_%d_%s" % (os.getpid(), uuid.uuid4().hex)]
+        srv = socket.socket(socket.AF_UNIX, socket.SOCK_STREAM)
+        srv.settimeout(timeout_s)
+        srv.bind(name[0])
+        srv.listen(max(1, world))
+    dist.broadcast_object_list(name, src=dist.get_global_rank(group, 0), group=group)
+    if rank == 0:
+        try:
+            for _ in range(world - 1):
+                conn, _ = srv.accept()
+                with conn:
+                    socket.send_fds(conn, [b"fd"], [fd])
+        finally:
+            srv.close()
+        return None
+    s = socket.socket(socket.AF_UNIX, socket.SOCK_STREAM)
+    s.settimeout(timeout_s)
+    try:
+        s.connect(name[0])
+        _, fds, _, _ = socket.recv_fds(s, 16, 1)
+    finally:
+        s.close()
+    if len(fds) != 1:
+        raise RuntimeError("share_fd: no descriptor received")
+    return fds[0]
+
+
 class NVLSAllReduce:
     def __init__(self, group, nbytes: int, device: torch.device):
         C = native()
@@ -64,38 +103,19 @@ class NVLSAllReduce:
 
     def _open(self, C) -> int:
         """Create (rank 0) or import (the others) the multicast object."""
-        name = [None]
-        srv = None
         if self.rank == 0:
             hid = C.nvls_create(self.device.index, self.world, self.size)
             fd = C.nvls_export_fd(hid)
-            name = ["\0femtotron_nvls_%d_%s" % (os.getpid(), uuid.uuid4().hex)]
-            srv = socket.socket(socket.AF_UNIX, socket.SOCK_STREAM)
-            srv.settimeout(120)
-            srv.bind(name[0])
-            srv.listen(self.world)
-        dist.broadcast_object_list(name, src=dist.get_global_rank(self.group, 0), group=self.group)
-        if self.rank == 0:
             try:
-                for _ in range(self.world - 1):
-                    conn, _ = srv.accept()
-                    with conn:
-                        socket.send_fds(conn, [b"nvls"], [fd])
+                share_fd(self.group, fd)
             finally:
-                srv.close()
                 os.close(fd)
             return hid
-        s = socket.socket(socket.AF_UNIX, socket.SOCK_STREAM)
-        s.settimeout(120)
-        s.connect(name[0])
+        fd = share_fd(self.group, None)
         try:
-            _, fds, _, _ = socket.recv_fds(s, 16, 1)
+            return C.nvls_import(self.device.index, self.world, self.size, fd)
         finally:
-            s.close()
-        try:
-            return C.nvls_import(self.device.index, self.world, self.size, fds[0])
-        finally:
-            os.close(fds[0])
+            os.close(fd)
 
     def _barrier(self) -> None:
         self.epoch += 1

@@ -1040,3 +1040,26 @@ def w_train_and_checkpoint(rank, world, tmpdir, tp, stage):
     with torch.no_grad():
         loss = tr.model(x, labels=x)["loss"].item()
     return {"loss": loss}
+
+
+def w_share_fd(rank, world, tmpdir):
+    """The descriptor hand-off of the NVLS set-up: rank 0's open file reaches every peer as a
+    working descriptor of the same file (read with pread at offset 0)."""
+    from femtotron_b200.parallel.nvls import share_fd
+    payload = b"multicast handle stand-in"
+    if rank == 0:
+        path = os.path.join(tmpdir, "fd_payload.bin")
+        with open(path, "wb") as f:
+            f.write(payload)
+        fd = os.open(path, os.O_RDONLY)
+        try:
+            got = share_fd(dist.group.WORLD, fd)
+        finally:
+            os.close(fd)
+        return {"rank0_returns_none": got is None}
+    fd = share_fd(dist.group.WORLD, None)
+    try:
+        data = os.pread(fd, len(payload), 0)
+    finally:
+        os.close(fd)
+    return {"received": data == payload}

@@ -234,3 +234,8 @@ def test_rank_leaving_makes_peers_fail_fast():
     res = run_ranks(W.w_rank_failure, 2, pg_timeout=5.0, timeout=120.0)
     assert res[1] == {"left": True}
     assert res[0]["raised"] and res[0]["elapsed"] < 60
+
+
+def test_share_fd_hands_a_descriptor_to_every_rank(tmp_path):
+    for r in run_ranks(W.w_share_fd, 3, str(tmp_path)):
+        assert all(r.values()), r
