@@ -67,6 +67,10 @@ struct Params {
   int gate_op;             // 0 none, 1 gate A rows, 2 gate B rows (K-major operands only)
   int gate_epoch;
   int64_t gate_off, gate_row_elems, gate_chunk_elems;
+  // Row rotation of the tile order (a multiple of 256 rows; 0 = none): tiles are visited
+  // starting at this output row, so a gated GEMM computes first on the rows that arrive first
+  // (the local chunk of an all-gather, then the peers' chunks in the order they are pulled).
+  int m_rot_rows;
   // Scatter epilogue (fused GEMM -> reduce-scatter): row r goes to owner o = r / scatter_rows,
   // stored at scatter_base[o] + (r - o * scatter_rows) * ldd (peer memory over NVLink).
   __nv_bfloat16* scatter_base[8];
@@ -115,6 +119,11 @@ __device__ __forceinline__ bool gate_wait(const Params& p, int64_t r0, int64_t r
   // data written by the copy engines is read next through the TMA (async) proxy
   asm volatile("fence.proxy.async.global;" ::: "memory");
   return true;
+}
+
+// Row-tile index after the tile-order rotation of Params::m_rot_rows (tiles of tile_rows rows).
+__device__ __forceinline__ int rotate_m(int tm, int tiles_m, int m_rot_rows, int tile_rows) {
+  return m_rot_rows ? (tm + m_rot_rows / tile_rows) % tiles_m : tm;
 }
 
 // Grouped tile order: walk group_m row-tiles down a column before moving right, so one
@@ -306,6 +315,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
         int tm, tn;
         tile_coords(t, tiles_m, tiles_n, p.group_m, tm, tn);
+        tm = rotate_m(tm, tiles_m, p.m_rot_rows, BM);
         const int m0 = tm * BM;
         const int n0 = tn * out_cols;
         if (p.gate_op == 1 && !gate_wait(p, m0, min(m0 + BM, p.M))) { ok = false; break; }
@@ -381,6 +391,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
       int tm, tn;
       tile_coords(t, tiles_m, tiles_n, p.group_m, tm, tn);
+      tm = rotate_m(tm, tiles_m, p.m_rot_rows, BM);
       const int m0 = tm * BM;
       const int n0 = tn * out_cols;
       if (!wait_bar(&s.acc_full[acc], acc_phase, p.err, 4)) break;
@@ -529,6 +540,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       for (int t = pair; t < num_tiles && ok; t += npairs) {
         int tm, tn;
         tile_coords(t, tiles_m, tiles_n, p.group_m, tm, tn);
+        tm = rotate_m(tm, tiles_m, p.m_rot_rows, 256);
         const int m0 = tm * 256 + static_cast<int>(rank) * 128;
         const int n0 = tn * out_cols;
         // K-major B rows held by this CTA (SwiGLU: leader = gate rows, peer = up rows)
@@ -619,6 +631,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     for (int t = pair; t < num_tiles; t += npairs) {
       int tm, tn;
       tile_coords(t, tiles_m, tiles_n, p.group_m, tm, tn);
+      tm = rotate_m(tm, tiles_m, p.m_rot_rows, 256);
       const int m0 = tm * 256 + static_cast<int>(rank) * 128;
       const int n0 = tn * out_cols;
       if (!wait_bar(&s.acc_full[acc], acc_phase, p.err, 16)) break;
@@ -727,6 +740,7 @@ struct GateScatter {
   int64_t gate_off = 0, gate_row_elems = 1, gate_chunk_elems = 1;
   std::vector<int64_t> scatter_ptrs;
   int scatter_rows = 0;
+  int64_t m_rot_rows = 0;
 };
 
 void gemm_tc_impl(const torch::Tensor& A, const torch::Tensor& B, torch::Tensor& D, bool a_mn,
@@ -744,14 +758,15 @@ void gemm_tc(const torch::Tensor& A, const torch::Tensor& B, torch::Tensor& D, b
 
 // Fused-communication GEMM: K-major operands, optional operand gate and scatter epilogue.
 //   gate_op 1/2 gates A/B rows on int32 flags at `gate_flags` (device address);
-//   mode 6 stores row r of D into scatter_ptrs[r / scatter_rows] (row stride D.stride(0)).
+//   mode 6 stores row r of D into scatter_ptrs[r / scatter_rows] (row stride D.stride(0));
+//   m_rot_rows (a multiple of 256, or 0) starts the tile order at that output row.
 void gemm_tc_fused(const torch::Tensor& A, const torch::Tensor& B, torch::Tensor& D, bool a_mn,
                    bool b_mn, int64_t mode,
                    const c10::optional<torch::Tensor>& R, const c10::optional<torch::Tensor>& GU,
                    int64_t gate_up_off, torch::Tensor& err, int64_t gate_flags, int64_t gate_op,
                    int64_t gate_epoch, int64_t gate_off, int64_t gate_row_elems,
                    int64_t gate_chunk_elems, const std::vector<int64_t>& scatter_ptrs,
-                   int64_t scatter_rows) {
+                   int64_t scatter_rows, int64_t m_rot_rows) {
   GateScatter gs;
   gs.gate_flags = gate_flags;
   gs.gate_op = static_cast<int>(gate_op);
@@ -761,6 +776,7 @@ void gemm_tc_fused(const torch::Tensor& A, const torch::Tensor& B, torch::Tensor
   gs.gate_chunk_elems = std::max<int64_t>(1, gate_chunk_elems);
   gs.scatter_ptrs = scatter_ptrs;
   gs.scatter_rows = static_cast<int>(scatter_rows);
+  gs.m_rot_rows = m_rot_rows;
   TORCH_CHECK(scatter_ptrs.size() <= 8, "gemm_tc_fused: at most 8 scatter owners");
   if (mode == 6) TORCH_CHECK(scatter_rows > 0 && !scatter_ptrs.empty(), "gemm_tc_fused: scatter needs owners");
   TORCH_CHECK(gs.gate_op == 0 || (gs.gate_op == 1 && !a_mn) || (gs.gate_op == 2 && !b_mn),
@@ -861,6 +877,8 @@ void gemm_tc_impl(const torch::Tensor& A, const torch::Tensor& B, torch::Tensor&
   p.gate_off = gs.gate_off;
   p.gate_row_elems = gs.gate_row_elems;
   p.gate_chunk_elems = gs.gate_chunk_elems;
+  // rotation in whole 256-row tiles (both the 128-row and the paired 256-row tilings)
+  p.m_rot_rows = (gs.m_rot_rows > 0 && gs.m_rot_rows % 256 == 0 && gs.m_rot_rows < M) ? gs.m_rot_rows : 0;
   for (int i = 0; i < 8; ++i)
     p.scatter_base[i] = i < static_cast<int>(gs.scatter_ptrs.size())
                             ? reinterpret_cast<__nv_bfloat16*>(gs.scatter_ptrs[i])

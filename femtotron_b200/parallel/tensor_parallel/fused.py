@@ -115,8 +115,12 @@ class TPFusedComm:
         return full, e
 
     def gate(self, epoch: int, rows_local: int, cols: int) -> dict:
+        """Operand gate of the consuming GEMM.  Its tiles start at this rank's own rows, the
+        chunk the pull kernel copies first, and follow the ring order of the pulls."""
+        rot = self.rank * rows_local
         return dict(gate_flags=self.local_flag("CHUNK", 0), gate_op=1, gate_epoch=epoch * self.ctas,
-                    gate_off=0, gate_row_elems=cols, gate_chunk_elems=rows_local * cols)
+                    gate_off=0, gate_row_elems=cols, gate_chunk_elems=rows_local * cols,
+                    gate_rot_rows=rot if rot % 256 == 0 else 0)
 
     def after_gated(self) -> None:
         """Order later work on the current stream after the pull kernel."""
@@ -168,7 +172,7 @@ def fused_gemm(a, b, out, *, a_mn=False, b_mn=False, mode="store_bf16", residual
     native().gemm_tc_fused(a, b, out, a_mn, b_mn, m, residual, gu, gate_up_off, error_flag(a.device),
                            g.get("gate_flags", 0), g.get("gate_op", 0), g.get("gate_epoch", 0),
                            g.get("gate_off", 0), g.get("gate_row_elems", 1), g.get("gate_chunk_elems", 1),
-                           list(ptrs), rows)
+                           list(ptrs), rows, g.get("gate_rot_rows", 0))
     return out
 
 

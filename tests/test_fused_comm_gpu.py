@@ -215,7 +215,7 @@ def test_ag_pull_gathers_every_chunk_and_feeds_the_gated_gemm():
         C.ag_pull([c.data_ptr() for c in chunks], [ready.data_ptr() + 4 * r for r in range(world)],
                   full, Tl * H * 2, count.data_ptr(), me, e, ctas, error_flag(dev), 5000)
     gate = dict(gate_flags=count.data_ptr(), gate_op=1, gate_epoch=e * ctas, gate_off=0,
-                gate_row_elems=H, gate_chunk_elems=Tl * H)
+                gate_row_elems=H, gate_chunk_elems=Tl * H, gate_rot_rows=me * Tl)
     fused_gemm(full, w, out, gate=gate)
     torch.cuda.current_stream().wait_stream(side)
     torch.cuda.current_stream().wait_stream(rel)
@@ -248,3 +248,17 @@ def test_rs_pull_sums_every_rank_partial_of_its_rows():
     torch.cuda.synchronize()
     with pytest.raises(KernelTimeoutError, match="code 243"):
         check_kernel_errors(dev)
+
+
+@pytest.mark.parametrize("M,N,K", [(1024, 768, 512), (2048, 4096, 1024), (1536, 256, 384), (4096, 1920, 640)])
+@pytest.mark.parametrize("rot", [256, 512, 768])
+def test_tile_order_rotation_keeps_the_product(M, N, K, rot):
+    """Starting the tile order at another row block (as the all-gather GEMM does, at its own
+    chunk) changes only the order in which tiles are computed."""
+    torch.manual_seed(6)
+    a = torch.randn(M, K, device=DEV, dtype=torch.bfloat16)
+    b = torch.randn(N, K, device=DEV, dtype=torch.bfloat16)
+    out = torch.empty(M, N, device=DEV, dtype=torch.bfloat16)
+    fused_gemm(a, b, out, gate=dict(gate_rot_rows=rot))
+    torch.cuda.synchronize()
+    assert rel_err(out, a.float() @ b.float().t()) < 1e-2
