@@ -1063,3 +1063,37 @@ def w_share_fd(rank, world, tmpdir):
     finally:
         os.close(fd)
     return {"received": data == payload}
+
+
+def w_zero3_variants(rank, world):
+    """ZeRO-3 loss curves with the per-step gather cache forced on and off, and with the free
+    parameters (embedding, final norm, LM head) sharded or replicated: the same math, so the
+    same losses; plus the memory effect of sharding the free parameters."""
+    cfg = tiny_config()
+    sd = full_state(cfg)
+    ctx = ctx_of(dp=world)
+    out = {}
+    saved = {k: os.environ.get(k) for k in ("FT_ZERO3_KEEP_IN_STEP", "FT_ZERO3_SHARD_FREE")}
+    try:
+        for keep in ("0", "1"):
+            for shard in ("0", "1"):
+                os.environ["FT_ZERO3_KEEP_IN_STEP"] = keep
+                os.environ["FT_ZERO3_SHARD_FREE"] = shard
+                tr = _build_trainer(cfg, sd, ctx, 3, steps=4, mb=2, ga=2, seed_data=3, ac=True)
+                st = tr.mp_manager.strategy
+                hist = tr.train()
+                t = torch.tensor([h["loss"] for h in hist])
+                dist.all_reduce(t)
+                state = sum(c.master.numel() for c in tr.mp_manager.clusters) + \
+                    sum(g.master.numel() for g in tr.mp_manager.groups if g.master is not None)
+                out[f"keep{keep}_shard{shard}"] = {"loss": (t / world).tolist(),
+                                                   "keep": st.keep_in_step,
+                                                   "free_clusters": len(st.free_clusters),
+                                                   "master_elems": state}
+    finally:
+        for k, v in saved.items():
+            if v is None:
+                os.environ.pop(k, None)
+            else:
+                os.environ[k] = v
+    return out

@@ -239,3 +239,14 @@ def test_rank_leaving_makes_peers_fail_fast():
 def test_share_fd_hands_a_descriptor_to_every_rank(tmp_path):
     for r in run_ranks(W.w_share_fd, 3, str(tmp_path)):
         assert all(r.values()), r
+
+
+def test_zero3_gather_cache_and_sharded_free_params_keep_the_losses():
+    r = run_ranks(W.w_zero3_variants, 2)[0]
+    base = r["keep0_shard0"]["loss"]
+    for key, v in r.items():
+        assert max(abs(a - b) for a, b in zip(v["loss"], base)) < 1e-5, (key, v["loss"], base)
+    assert r["keep1_shard0"]["keep"] and not r["keep0_shard0"]["keep"]
+    assert r["keep0_shard1"]["free_clusters"] == 3 and r["keep0_shard0"]["free_clusters"] == 0
+    # sharding the free parameters halves their fp32 masters at DP=2
+    assert r["keep0_shard1"]["master_elems"] < r["keep0_shard0"]["master_elems"]
