@@ -242,6 +242,45 @@ def op_rs_p2p(name):
     return {"kind": "bytes", "bytes": shard * (4 * R + 12 + 16 + 2), "run": run, "name": name}
 
 
+def op_tp_ag_pull(name, world=8):
+    """The tensor-parallel all-gather pull kernel alone (``ag_pull``) with every "peer" chunk
+    in local memory: Llama-2-13B, TP=8 + SP, 1024 tokens x 5120 per rank; READY flags preset."""
+    C = native()
+    from femtotron_b200.ops.ext import error_flag
+    Tl, H = 1024, 5120
+    chunks = [torch.randn(Tl, H, device="cuda").to(torch.bfloat16) for _ in range(world)]
+    full = torch.empty(world * Tl, H, device="cuda", dtype=torch.bfloat16)
+    ready = torch.ones(world, dtype=torch.int32, device="cuda")
+    count = torch.zeros(world, dtype=torch.int32, device="cuda")
+    ctas = int(C.gate_reserved_sms())
+    ptrs = [c.data_ptr() for c in chunks]
+
+    def run():
+        C.ag_pull(ptrs, [ready.data_ptr() + 4 * r for r in range(world)], full, Tl * H * 2,
+                  count.data_ptr(), 0, 1, ctas, error_flag(full.device), 1000)
+    run.keep = chunks
+    return {"kind": "bytes", "bytes": 2 * world * Tl * H * 2, "run": run, "name": name}
+
+
+def op_tp_rs_pull(name, world=8):
+    """The tensor-parallel reduce-scatter pull (``rs_pull``) with every rank's partial in
+    local memory: this rank's 1024 rows x 5120 of eight partials, plus the residual."""
+    C = native()
+    from femtotron_b200.ops.ext import error_flag
+    Tl, N = 1024, 5120
+    parts = [torch.randn(Tl, N, device="cuda").to(torch.bfloat16) for _ in range(world)]
+    resid = torch.randn(Tl, N, device="cuda").to(torch.bfloat16)
+    out = torch.empty(Tl, N, device="cuda", dtype=torch.bfloat16)
+    flags = torch.ones(world, dtype=torch.int32, device="cuda")
+    ptrs = [p.data_ptr() for p in parts]
+
+    def run():
+        C.rs_pull(ptrs, [flags.data_ptr() + 4 * r for r in range(world)], resid.reshape(-1), out,
+                  Tl * N, 1, error_flag(out.device), 1000)
+    run.keep = parts
+    return {"kind": "bytes", "bytes": (world + 2) * Tl * N * 2, "run": run, "name": name}
+
+
 OPS = {
     "p2p_copy_1": lambda: op_p2p_copy("p2p_copy_1", 1),
     "p2p_copy_4": lambda: op_p2p_copy("p2p_copy_4", 4),
@@ -267,6 +306,8 @@ OPS = {
     "gemm_gated_ag": lambda: op_gemm_gated("gemm_gated_ag"),
     "gemm_scatter_rs": lambda: op_gemm_scatter("gemm_scatter_rs"),
     "rs_p2p": lambda: op_rs_p2p("rs_p2p"),
+    "tp_ag_pull": lambda: op_tp_ag_pull("tp_ag_pull"),
+    "tp_rs_pull": lambda: op_tp_rs_pull("tp_rs_pull"),
     "xent_stats": lambda: op_xent("xent_stats"),
 }
 
