@@ -44,7 +44,7 @@ void gemm_tc_fused(const torch::Tensor& A, const torch::Tensor& B, torch::Tensor
                    int64_t gate_up_off, torch::Tensor& err, int64_t gate_flags, int64_t gate_op,
                    int64_t gate_epoch, int64_t gate_off, int64_t gate_row_elems,
                    int64_t gate_chunk_elems, const std::vector<int64_t>& scatter_ptrs,
-                   int64_t scatter_rows, int64_t m_rot_rows);
+                   int64_t scatter_rows, int64_t m_rot_rows, int64_t reserved_sms);
 void wait_flags_geq(const std::vector<int64_t>& addrs, int64_t value, torch::Tensor& err,
                     int64_t timeout_ms, int64_t code);
 void rs_adamw(const std::vector<int64_t>& src_ptrs, int64_t base, int64_t n, bool src_f32,

@@ -67,6 +67,8 @@ struct Params {
   int gate_op;             // 0 none, 1 gate A rows, 2 gate B rows (K-major operands only)
   int gate_epoch;
   int64_t gate_off, gate_row_elems, gate_chunk_elems;
+  // SMs a gated launch leaves free for the kernels that release its gate (0: the default)
+  int reserved_sms;
   // Row rotation of the tile order (a multiple of 256 rows; 0 = none): tiles are visited
   // starting at this output row, so a gated GEMM computes first on the rows that arrive first
   // (the local chunk of an all-gather, then the peers' chunks in the order they are pulled).
@@ -672,14 +674,17 @@ static int num_sms() {
   return n;
 }
 
-// A gated GEMM (fused all-gather) waits for chunks that the pull kernel (tp_comm.cu) brings
-// in from the peers on a side stream, one CTA per SM.  A persistent grid over every SM could
-// leave that kernel no SM to run on while the GEMM waits for it, so gated launches leave
-// GATE_RESERVED_SMS SMs free, and the pull kernel runs exactly that many CTAs.
+// A gated GEMM (fused all-gather) waits for chunks that other streams bring in: the pull
+// kernel (tp_comm.cu, one CTA per SM) or copy engines after one-warp flag waits.  A
+// persistent grid over every SM could leave those kernels no SM to run on while the GEMM waits
+// for them, so gated launches leave SMs free: Params::reserved_sms, or GATE_RESERVED_SMS (the
+// pull kernel's CTA count) when the caller gives none.
 constexpr int GATE_RESERVED_SMS = 16;
 
 static int usable_sms(const Params& p) {
-  return p.gate_op != 0 ? std::max(2, num_sms() - GATE_RESERVED_SMS) : num_sms();
+  if (p.gate_op == 0) return num_sms();
+  const int keep = p.reserved_sms > 0 ? p.reserved_sms : GATE_RESERVED_SMS;
+  return std::max(2, num_sms() - keep);
 }
 
 template <bool A_MN, bool B_MN, int BN, int STAGES>
@@ -741,6 +746,7 @@ struct GateScatter {
   std::vector<int64_t> scatter_ptrs;
   int scatter_rows = 0;
   int64_t m_rot_rows = 0;
+  int reserved_sms = 0;
 };
 
 void gemm_tc_impl(const torch::Tensor& A, const torch::Tensor& B, torch::Tensor& D, bool a_mn,
@@ -759,14 +765,15 @@ void gemm_tc(const torch::Tensor& A, const torch::Tensor& B, torch::Tensor& D, b
 // Fused-communication GEMM: K-major operands, optional operand gate and scatter epilogue.
 //   gate_op 1/2 gates A/B rows on int32 flags at `gate_flags` (device address);
 //   mode 6 stores row r of D into scatter_ptrs[r / scatter_rows] (row stride D.stride(0));
-//   m_rot_rows (a multiple of 256, or 0) starts the tile order at that output row.
+//   m_rot_rows (a multiple of 256, or 0) starts the tile order at that output row;
+//   reserved_sms (> 0) is how many SMs a gated launch leaves to the streams releasing it.
 void gemm_tc_fused(const torch::Tensor& A, const torch::Tensor& B, torch::Tensor& D, bool a_mn,
                    bool b_mn, int64_t mode,
                    const c10::optional<torch::Tensor>& R, const c10::optional<torch::Tensor>& GU,
                    int64_t gate_up_off, torch::Tensor& err, int64_t gate_flags, int64_t gate_op,
                    int64_t gate_epoch, int64_t gate_off, int64_t gate_row_elems,
                    int64_t gate_chunk_elems, const std::vector<int64_t>& scatter_ptrs,
-                   int64_t scatter_rows, int64_t m_rot_rows) {
+                   int64_t scatter_rows, int64_t m_rot_rows, int64_t reserved_sms) {
   GateScatter gs;
   gs.gate_flags = gate_flags;
   gs.gate_op = static_cast<int>(gate_op);
@@ -777,6 +784,7 @@ void gemm_tc_fused(const torch::Tensor& A, const torch::Tensor& B, torch::Tensor
   gs.scatter_ptrs = scatter_ptrs;
   gs.scatter_rows = static_cast<int>(scatter_rows);
   gs.m_rot_rows = m_rot_rows;
+  gs.reserved_sms = static_cast<int>(std::max<int64_t>(0, reserved_sms));
   TORCH_CHECK(scatter_ptrs.size() <= 8, "gemm_tc_fused: at most 8 scatter owners");
   if (mode == 6) TORCH_CHECK(scatter_rows > 0 && !scatter_ptrs.empty(), "gemm_tc_fused: scatter needs owners");
   TORCH_CHECK(gs.gate_op == 0 || (gs.gate_op == 1 && !a_mn) || (gs.gate_op == 2 && !b_mn),
@@ -878,6 +886,7 @@ void gemm_tc_impl(const torch::Tensor& A, const torch::Tensor& B, torch::Tensor&
   p.gate_row_elems = gs.gate_row_elems;
   p.gate_chunk_elems = gs.gate_chunk_elems;
   // rotation in whole 256-row tiles (both the 128-row and the paired 256-row tilings)
+  p.reserved_sms = gs.reserved_sms;
   p.m_rot_rows = (gs.m_rot_rows > 0 && gs.m_rot_rows % 256 == 0 && gs.m_rot_rows < M) ? gs.m_rot_rows : 0;
   for (int i = 0; i < 8; ++i)
     p.scatter_base[i] = i < static_cast<int>(gs.scatter_ptrs.size())

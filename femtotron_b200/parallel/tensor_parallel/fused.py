@@ -5,15 +5,17 @@ All-gather (AG) of a token-sharded activation x_local [Tl, H] into x_full [T = t
   1. after a bounded wait for every peer's DONE flag of two epochs ago (they finished reading
      this slot), the rank stages x_local in its symmetric slot and writes epoch e into every
      peer's READY[me] flag (stream memory write, system-scope fence first);
-  2. on a side stream the pull kernel (``ag_pull``, one CTA on each of the SMs the gated GEMM
-     leaves free) visits the ranks in ring order starting with itself, waits (bounded) for the
-     owner's READY flag, copies the owner's chunk over NVLink into x_full with wide loads and
-     bumps the chunk's local counter; afterwards the stream writes DONE[me] = e into every
-     peer;
-  3. the consuming GEMM runs on the compute stream at once: its TMA producer waits (bounded)
-     until the counter of every chunk its tile rows touch reaches e x CTAs, so MMAs on the
-     local chunk start immediately and peer rows are consumed as they land; every remote row
-     crosses NVLink exactly once.
+  2. every chunk is brought into x_full on its own stream, one stream per rank in ring order
+     starting with this rank: a one-warp kernel waits (bounded) for the owner's READY flag,
+     the copy engines pull the chunk over NVLink (so several engines run at once and no SM
+     moves bytes), and a stream write sets the chunk's flag to e; once every chunk is in, a
+     stream writes DONE[me] = e into every peer (FT_TP_AG=sm instead runs ``ag_pull``, a pull
+     kernel on the SMs the GEMM leaves free, which bumps per-chunk counters);
+  3. the consuming GEMM runs on the compute stream at once, leaving two SMs to the flag waits:
+     its TMA producer waits (bounded) until the flag of every chunk its tile rows touch has
+     reached e, its tiles start at this rank's own rows and follow the ring order, so MMAs on
+     the local chunk start immediately and peer rows are consumed as they land; every remote
+     row crosses NVLink exactly once.
 Reduce-scatter (RS) of a row-parallel GEMM's partial output over tokens:
   1. after a bounded wait for every peer's CONS flag of two epochs ago, the GEMM stores its
      full partial [T, N] into this rank's symmetric slot (local stores) and the stream writes
@@ -27,8 +29,9 @@ the same sequence of calls, so stale flags are never mistaken for fresh ones.
 Every wait is a kernel with a time limit (FT_COMM_TIMEOUT_MS, default 30 s): a peer that never
 publishes makes the waiting rank record an error code (200 + flag-kind offset + peer) and
 continue, and the host raises KernelTimeoutError at its next ``check_kernel_errors``.  The
-gated GEMM leaves ``gate_reserved_sms()`` SMs free, and the pull kernel runs exactly that many
-CTAs, so the two always run side by side.
+gated GEMM leaves SMs free for the kernels that release it (two for the flag waits of the
+copy-engine mode, ``gate_reserved_sms()`` for the pull kernel), so they always run side by
+side.
 """
 from __future__ import annotations
 
@@ -46,6 +49,8 @@ NSLOTS = 2
 COMM_TIMEOUT_MS = int(os.environ.get("FT_COMM_TIMEOUT_MS", "30000"))
 # error code base per waited flag kind (code = base + index of the first missing peer)
 WAIT_CODES = {"READY": 200, "DONE": 220, "PART": 240, "CONS": 260}
+# SMs a gated GEMM leaves to the one-warp flag waits of the copy-engine all-gather
+CE_RESERVED_SMS = 2
 
 
 class TPFusedComm:
@@ -61,7 +66,13 @@ class TPFusedComm:
         self.off_flags = a.reserve("flags", len(KINDS) * 64 * 4)
         self.heap = SymmetricHeap(group, None, a.size, device)
         self.cs = torch.cuda.Stream(device=device)
-        self.ctas = int(native().gate_reserved_sms())
+        # all-gather mover: copy engines, one stream per chunk ("ce"), or the SM pull kernel
+        self.ag_mode = os.environ.get("FT_TP_AG", "ce")
+        if self.ag_mode == "sm":
+            self.ctas = int(native().gate_reserved_sms())
+        else:
+            self.ctas = CE_RESERVED_SMS
+            self.pull_streams = [torch.cuda.Stream(device=device) for _ in range(world)]
         self.ag_epoch = 0
         self.rs_epoch = 0
 
@@ -104,26 +115,45 @@ class TPFusedComm:
         self.heap.view(slot_off, Tl * H, torch.bfloat16).copy_(x_local.reshape(-1))
         self.publish("READY", e)
         full = torch.empty(self.world * Tl, H, dtype=torch.bfloat16, device=self.device)
-        self.cs.wait_stream(cur)
+        C = native()
+        if self.ag_mode == "sm":
+            self.cs.wait_stream(cur)
+            with torch.cuda.stream(self.cs):
+                C.ag_pull([self.heap.peer_ptr(r, slot_off) for r in range(self.world)],
+                          [self.local_flag("READY", r) for r in range(self.world)],
+                          full, Tl * H * 2, self.local_flag("CHUNK", 0), self.rank, e,
+                          self.ctas, error_flag(self.device), COMM_TIMEOUT_MS)
+                self.publish("DONE", e)
+            full.record_stream(self.cs)
+            return full, e
+        nb = Tl * H * 2
+        for k in range(self.world):
+            r = (self.rank + k) % self.world
+            st = self.pull_streams[k]
+            st.wait_stream(cur)
+            with torch.cuda.stream(st):
+                if r != self.rank:
+                    C.wait_flags_geq([self.local_flag("READY", r)], e, error_flag(self.device),
+                                     COMM_TIMEOUT_MS, WAIT_CODES["READY"] + r)
+                C.copy_from_ptrs([full.data_ptr() + r * nb], [self.heap.peer_ptr(r, slot_off)], [nb])
+                C.stream_write(self.local_flag("CHUNK", r), e)
+            full.record_stream(st)
+            self.cs.wait_stream(st)
         with torch.cuda.stream(self.cs):
-            native().ag_pull([self.heap.peer_ptr(r, slot_off) for r in range(self.world)],
-                             [self.local_flag("READY", r) for r in range(self.world)],
-                             full, Tl * H * 2, self.local_flag("CHUNK", 0), self.rank, e,
-                             self.ctas, error_flag(self.device), COMM_TIMEOUT_MS)
-            self.publish("DONE", e)
-        full.record_stream(self.cs)
+            self.publish("DONE", e)      # every peer's slot read: the owners may reuse it
         return full, e
 
     def gate(self, epoch: int, rows_local: int, cols: int) -> dict:
         """Operand gate of the consuming GEMM.  Its tiles start at this rank's own rows, the
         chunk the pull kernel copies first, and follow the ring order of the pulls."""
         rot = self.rank * rows_local
-        return dict(gate_flags=self.local_flag("CHUNK", 0), gate_op=1, gate_epoch=epoch * self.ctas,
+        target = epoch * self.ctas if self.ag_mode == "sm" else epoch   # counters or epochs
+        return dict(gate_flags=self.local_flag("CHUNK", 0), gate_op=1, gate_epoch=target,
                     gate_off=0, gate_row_elems=cols, gate_chunk_elems=rows_local * cols,
-                    gate_rot_rows=rot if rot % 256 == 0 else 0)
+                    gate_rot_rows=rot if rot % 256 == 0 else 0, gate_reserved=self.ctas)
 
     def after_gated(self) -> None:
-        """Order later work on the current stream after the pull kernel."""
+        """Order later work on the current stream after every chunk's transfer."""
         torch.cuda.current_stream(self.device).wait_stream(self.cs)
 
     # ------------------------------------------------------------------ reduce-scatter
@@ -172,7 +202,7 @@ def fused_gemm(a, b, out, *, a_mn=False, b_mn=False, mode="store_bf16", residual
     native().gemm_tc_fused(a, b, out, a_mn, b_mn, m, residual, gu, gate_up_off, error_flag(a.device),
                            g.get("gate_flags", 0), g.get("gate_op", 0), g.get("gate_epoch", 0),
                            g.get("gate_off", 0), g.get("gate_row_elems", 1), g.get("gate_chunk_elems", 1),
-                           list(ptrs), rows, g.get("gate_rot_rows", 0))
+                           list(ptrs), rows, g.get("gate_rot_rows", 0), g.get("gate_reserved", 0))
     return out
 
 
