@@ -472,7 +472,11 @@ def run_reference(args):
           "e2e": {"value": tokens / (wall / 1e3), "unit": "tokens/s", "ms_per_step": wall,
                   "h2d_bytes_per_step": ga * rows * S * 8 * 2, "d2h_bytes_per_step": 4},
           "peak_mem_gb": round(max_over_ranks(torch.cuda.max_memory_allocated(device) / 2 ** 30), 1),
-          "impl": "reference", "clocks": clk.summary()})
+          "impl": "reference", "clocks": clk.summary(),
+          **({"notes": "the reference's activation checkpointing calls torch checkpoint with "
+                       "debug=True (femtotron/training/activation_ckpt.py:84), which records "
+                       "every op with its tracebacks; its step is host-bound"}
+             if cfg["ac_enabled"] else {})})
     dist.barrier()
     dist.destroy_process_group()
 
