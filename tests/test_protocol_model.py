@@ -1,7 +1,8 @@
 """Model check, on the CPU, of the cross-GPU flag protocols that order this library's NVLink
 traffic: the sequence-parallel all-gather -> GEMM and GEMM -> reduce-scatter of
 ``parallel/tensor_parallel/fused.py`` (both all-gather movers) and the ZeRO-3 gradient
-reduce-scatter of ``sharding/param_group_cluster.py::_reduce_symm``.
+reduce-scatter of ``sharding/param_group_cluster.py::_reduce_symm`` and the in-switch (NVLS)
+all-reduce of ``parallel/nvls.py``.
 
 The real Python code of those classes runs for every simulated rank; only the device is
 replaced.  Each CUDA stream becomes a FIFO of operations, and each native call becomes the
@@ -121,11 +122,14 @@ class Sim:
         owner, off = decode(a)
         return (owner,) + self.locate(off)
 
-    def write_slot(self, key, epoch: int, writer: int) -> Op:
+    def write_slot(self, key, epoch, writer: int, needed=None) -> Op:
+        """Stream write of `epoch` into a slot; `needed(old)`: the ranks that must have read
+        the old content first (default: every rank)."""
         def run():
             old = self.version.get(key)
-            if old is not None:
-                missing = set(range(self.world)) - self.readers[(key, old)]
+            if old is not None and old != epoch:
+                must = set(range(self.world)) if needed is None else needed(old)
+                missing = must - self.readers[(key, old)]
                 if missing:
                     raise Violation(f"rank {writer} overwrote {key} with epoch {epoch} before "
                                     f"ranks {sorted(missing)} read epoch {old}")
@@ -540,3 +544,144 @@ def test_tp_back_to_back_all_gathers_reuse_slots_safely(monkeypatch, mode):
             monkeypatch.undo()
     assert found is not None, "no interleaving showed the missing DONE ordering"
     assert "overwrote" in str(found) or "holding" in str(found), found
+
+
+# =============================================================== NVLS all-reduce
+class FakeTensor:
+    """A user tensor handed to the NVLS all-reduce: copying into it reads this rank's copy of
+    the multicast buffer (every slice must hold the round's reduced result)."""
+    dtype = torch.float32
+
+    def __init__(self, sim, ar, numel):
+        self.sim, self.ar, self._n = sim, ar, numel
+
+    def is_contiguous(self):
+        return True
+
+    def numel(self):
+        return self._n
+
+    def element_size(self):
+        return 4
+
+    def reshape(self, *shape):
+        return self
+
+    def view(self, *shape):
+        return self
+
+    def copy_(self, src):
+        sim, ar, me = self.sim, self.ar, self.sim.rank
+        k = ar.epoch // 2          # after the round's two barriers
+
+        def run():
+            for j in range(sim.world):
+                sim.read_slot((me, "copy", j), ("out", k), me)
+        sim.put(Op(f"copy out round {k}", run))
+        return self
+
+
+class FakeBuf:
+    """This rank's copy of the multicast buffer: writing into it stages the round's input."""
+
+    def __init__(self, sim, ar):
+        self.sim, self.ar = sim, ar
+
+    def __getitem__(self, idx):
+        return self
+
+    def view(self, dtype):
+        return self
+
+    def copy_(self, src):
+        sim, ar, me = self.sim, self.ar, self.sim.rank
+        k = ar.epoch // 2 + 1      # before the round's first barrier
+        for j in range(sim.world):
+            # the old input of slice j must have been reduced by rank j, an old result read
+            # back by this rank
+            sim.put(sim.write_slot((me, "copy", j), ("in", k), me,
+                                   needed=lambda old, j=j: {j} if old[0] == "in" else {me}))
+        return self
+
+
+def build_nvls(monkeypatch, world: int, control=None):
+    from femtotron_b200.parallel import nvls
+    sim = Sim(world)
+    nat = FakeNative(sim)
+    patch_device(monkeypatch, sim, nat)
+    monkeypatch.setattr(nvls, "native", lambda: nat)
+    monkeypatch.setattr(nvls, "error_flag", lambda dev: None)
+    ars = []
+    for r in range(world):
+        sim.rank = r
+        sim.cur[r] = sim.new_stream()
+        ar = object.__new__(nvls.NVLSAllReduce)
+        ar.__dict__.update(group=None, rank=r, world=world, device=torch.device("cpu"),
+                           size=1 << 20, data_bytes=(1 << 20) - 4096, flag_off=(1 << 20) - 4096,
+                           uc=addr(r, 0), mc=0, epoch=0, closed=False)
+        ar.buf = FakeBuf(sim, ar)
+        ars.append(ar)
+    skipped = {"no_first_barrier": 1, "no_second_barrier": 0}.get(control)
+
+    def nvls_barrier(uc, mc, flag_off, target, err, code, timeout_ms):
+        me = sim.rank
+        ar = ars[me]
+
+        def arrive():                   # multimem.red.add of 1 into every rank's counter
+            for a in range(world):
+                sim.flags[("ctr", a)] += 1
+        sim.put(Op(f"barrier arrive {target}", arrive))
+        if skipped is not None and ar.epoch % 2 == skipped:
+            return                      # negative control: arrive without waiting
+        sim.put(Op(f"barrier wait {target}", ready=lambda: sim.flags[("ctr", me)] >= target))
+
+    def nvls_reduce_slice(mc, nbytes, rank, world_, f32, scale):
+        k = (ars[rank].epoch + 1) // 2
+
+        def run():                      # multimem.ld_reduce of slice `rank`, multimem.st back
+            for a in range(world):
+                sim.read_slot((a, "copy", rank), ("in", k), rank)
+            for a in range(world):
+                sim.write_slot((a, "copy", rank), ("out", k), rank,
+                               needed=lambda old: {rank}).run()
+        sim.put(Op(f"reduce slice {rank} round {k}", run))
+    nat.nvls_barrier = nvls_barrier
+    nat.nvls_reduce_slice = nvls_reduce_slice
+    return sim, ars
+
+
+def run_nvls(monkeypatch, world, seed, rounds=6, control=None):
+    sim, ars = build_nvls(monkeypatch, world, control)
+    kinds = random.Random(1000 + seed).choices(["one", "many"], k=rounds)  # same on every rank
+    for r, ar in enumerate(ars):
+        sim.rank = r
+        for kind in kinds:
+            if kind == "one":
+                ar.all_reduce_(FakeTensor(sim, ar, 1024))
+            else:
+                ar.all_reduce_many_([FakeTensor(sim, ar, 256), FakeTensor(sim, ar, 512)],
+                                    average=True)
+    sim.run(random.Random(seed))
+    assert all(ar.epoch == 2 * rounds for ar in ars)
+    return sim
+
+
+@pytest.mark.parametrize("world,seeds", [(2, 60), (4, 40), (8, 15)])
+def test_nvls_all_reduce_protocol_is_race_and_deadlock_free(monkeypatch, world, seeds):
+    for seed in range(seeds):
+        run_nvls(monkeypatch, world, seed)
+        monkeypatch.undo()
+
+
+@pytest.mark.parametrize("control", ["no_first_barrier", "no_second_barrier"])
+def test_nvls_checker_catches_a_missing_barrier(monkeypatch, control):
+    found = None
+    for seed in range(80):
+        try:
+            run_nvls(monkeypatch, 4, seed, control=control)
+        except Violation as e:
+            found = e
+            break
+        finally:
+            monkeypatch.undo()
+    assert found is not None, f"{control}: no interleaving showed the missing barrier"
