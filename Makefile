@@ -2,7 +2,8 @@
 #
 #   make build            compile the sm_100a extension in-tree
 #   make test             CPU suite: units + multi-rank gloo (TP/SP, ZeRO-0..3, PP, resume, failures)
-#   make test-unit        pure unit tests only
+#   make test-unit        pure unit tests only (incl. benchmark configurations, clock sampler)
+#   make test-race        model check of the cross-GPU flag protocols (random interleavings)
 #   make test-integration multi-rank CPU tests and the CLI
 #   make test-quick       unit tests + the 2-rank ZeRO stage and TP equivalence checks
 #   make test-gpu         kernels, model and bounded-wait tests on a B200 (pytest -m gpu)
@@ -16,7 +17,7 @@ GPUS ?= 1
 TIMEOUT ?= 1800
 PORT ?= 29511
 
-.PHONY: build test test-unit test-integration test-quick test-gpu bench train-tiny clean
+.PHONY: build test test-unit test-race test-integration test-quick test-gpu bench train-tiny clean
 
 build:
 	$(PYTHON) setup.py build_ext --inplace
@@ -25,7 +26,11 @@ test:
 	timeout $(TIMEOUT) $(PYTHON) -m pytest tests -q -m "not gpu"
 
 test-unit:
-	timeout $(TIMEOUT) $(PYTHON) -m pytest tests/test_units.py tests/test_model_vs_hf.py -q
+	timeout $(TIMEOUT) $(PYTHON) -m pytest tests/test_units.py tests/test_model_vs_hf.py \
+		tests/test_bench_config.py tests/test_clocks.py -q
+
+test-race:
+	timeout $(TIMEOUT) $(PYTHON) -m pytest tests/test_protocol_model.py -q
 
 test-integration:
 	timeout $(TIMEOUT) $(PYTHON) -m pytest tests/test_distributed_cpu.py tests/test_cli.py -q

@@ -29,8 +29,6 @@ void adamw_multi(const std::vector<torch::Tensor>& params, const std::vector<tor
                  const c10::optional<torch::Tensor>& grad_scale);
 void sumsq_multi(const std::vector<torch::Tensor>& xs, const std::vector<int64_t>& slots,
                  torch::Tensor& out);
-void clip_coef(const torch::Tensor& sumsq, torch::Tensor& norm_out, torch::Tensor& coef_out,
-               double max_norm, double extra_scale);
 torch::Tensor symm_alloc(int64_t nbytes, int64_t device);
 torch::Tensor ipc_handle(const torch::Tensor& t);
 int64_t ipc_open(const torch::Tensor& handle, int64_t device);
@@ -97,7 +95,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("embed_bwd", &ft::embed_bwd);
   m.def("adamw_multi", &ft::adamw_multi);
   m.def("sumsq_multi", &ft::sumsq_multi);
-  m.def("clip_coef", &ft::clip_coef);
   m.def("symm_alloc", &ft::symm_alloc);
   m.def("ipc_handle", &ft::ipc_handle);
   m.def("ipc_open", &ft::ipc_open);

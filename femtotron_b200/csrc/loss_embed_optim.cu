@@ -263,14 +263,6 @@ __global__ void sumsq_kernel(const SqSeg* __restrict__ segs, const int2* __restr
   }
 }
 
-// clip coefficient: coef = min(1, max_norm / (sqrt(sumsq) + 1e-6)); also exports the norm.
-__global__ void clip_coef_kernel(const float* __restrict__ sumsq, float* __restrict__ norm_out,
-                                 float* __restrict__ coef_out, float max_norm, float extra_scale) {
-  const float n = sqrtf(sumsq[0]);
-  norm_out[0] = n;
-  coef_out[0] = fminf(1.f, max_norm / (n + 1e-6f)) * extra_scale;
-}
-
 int sm_count() {
   int dev, sms;
   cudaGetDevice(&dev);
@@ -442,15 +434,6 @@ void sumsq_multi(const std::vector<torch::Tensor>& xs, const std::vector<int64_t
                         [&](const SqSeg* s, const int2* c, const int64_t* o, int nc) {
                           sumsq_kernel<<<nc, 512, 0, st>>>(s, c, o, op, CH);
                         });
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
-}
-
-void clip_coef(const torch::Tensor& sumsq, torch::Tensor& norm_out, torch::Tensor& coef_out,
-               double max_norm, double extra_scale) {
-  const c10::cuda::CUDAGuard g(sumsq.device());
-  clip_coef_kernel<<<1, 1, 0, at::cuda::getCurrentCUDAStream()>>>(
-      sumsq.data_ptr<float>(), norm_out.data_ptr<float>(), coef_out.data_ptr<float>(),
-      static_cast<float>(max_norm), static_cast<float>(extra_scale));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

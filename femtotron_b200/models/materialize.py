@@ -83,21 +83,3 @@ def materialize_model(model: nn.Module, device, dtype=torch.bfloat16, init_std: 
                 tmp.normal_(mean=0.0, std=init_std)
                 p.copy_(tmp)
     return model
-
-
-def unit_flat_view(params) -> torch.Tensor | None:
-    """The flat 1-D storage spanned by consecutive parameters, or None."""
-    params = list(params)
-    if not params:
-        return None
-    first = params[0]
-    st = first.untyped_storage().data_ptr()
-    ptr = first.data_ptr()
-    for p in params:
-        if p.untyped_storage().data_ptr() != st or p.data_ptr() != ptr or not p.is_contiguous():
-            return None
-        ptr += p.numel() * p.element_size()
-    total = sum(p.numel() for p in params)
-    v = torch.empty(0, dtype=first.dtype, device=first.device)
-    v.set_(first.untyped_storage(), first.storage_offset(), (total,), (1,))
-    return v
