@@ -32,6 +32,7 @@ from __future__ import annotations
 
 import os
 import time
+import warnings
 from contextlib import contextmanager
 
 import torch
@@ -432,8 +433,8 @@ class ZeRO3Strategy:
                 c._grad_buffer = None
                 c.in_backward = False
                 c.reshard()
-            except Exception:
-                pass
+            except Exception as e:      # recovery must not mask the error being handled
+                warnings.warn(f"ZeRO-3 recovery could not reset cluster {c.name}: {e!r}")
 
     def summary(self) -> dict:
         cs = self.clusters + self.free_clusters
