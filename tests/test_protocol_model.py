@@ -476,12 +476,17 @@ def build_zero(monkeypatch, world: int, units: int, early: bool):
     return sim, nat, ranks
 
 
-def zero_program(sim: Sim, nat: FakeNative, cur, rs, clusters, steps: int, barrier=True):
-    """Per step: the units' backward (last unit first), each followed by its reduce-scatter
-    (``_reduce_symm``, the real method), then ``wait_comm`` and the ``post_step`` barrier."""
+def zero_program(sim: Sim, nat: FakeNative, cur, rs, clusters, steps: int, barrier=True,
+                 order_rng=None):
+    """Per step: the units' backward (last unit first, or a per-rank random order with
+    `order_rng`), each followed by its reduce-scatter (``_reduce_symm``, the real method), then
+    ``wait_comm`` and the ``post_step`` barrier."""
     r = sim.rank
     for _step in range(steps):
-        for c in reversed(clusters):
+        order = list(reversed(clusters))
+        if order_rng is not None:
+            order_rng.shuffle(order)
+        for c in order:
             # the backward writes this rank's unsharded gradient buffer of the unit
             sim.put(sim.write_slot((r, "grad", c.grad_offset >> 20), c._rs_epoch + 1, r))
             nat.zero_epoch = lambda c=c: c._rs_epoch
@@ -491,14 +496,16 @@ def zero_program(sim: Sim, nat: FakeNative, cur, rs, clusters, steps: int, barri
             sim.barrier()            # post_step: one all-reduce on the compute stream
 
 
-def run_zero(monkeypatch, world, seed, units=3, steps=3, early=False, control=None):
+def run_zero(monkeypatch, world, seed, units=3, steps=3, early=False, control=None,
+             shuffled=False):
     sim, nat, ranks = build_zero(monkeypatch, world, units, early)
     if control == "no_flag_wait":
         from femtotron_b200.sharding.param_group_cluster import RS_WAIT_CODE
         nat.skip_wait_codes.add(RS_WAIT_CODE)
     for r, (cur, rs, cl) in enumerate(ranks):
         sim.rank = r
-        zero_program(sim, nat, cur, rs, cl, steps, barrier=control != "no_barrier")
+        zero_program(sim, nat, cur, rs, cl, steps, barrier=control != "no_barrier",
+                     order_rng=random.Random(seed * 97 + r) if shuffled else None)
     sim.run(random.Random(seed))
     for (cur, rs, cl) in ranks:
         assert all(c._rs_epoch == steps for c in cl)
@@ -510,6 +517,15 @@ def run_zero(monkeypatch, world, seed, units=3, steps=3, early=False, control=No
 def test_zero3_reduce_scatter_protocol_is_race_and_deadlock_free(monkeypatch, world, seeds, early):
     for seed in range(seeds):
         run_zero(monkeypatch, world, seed, early=early)
+        monkeypatch.undo()
+
+
+def test_zero3_reduce_scatter_does_not_depend_on_a_common_unit_order(monkeypatch):
+    """Every unit has its own flags and epochs, and the flags are published from the compute
+    stream, which never waits for the reduce stream before the step's end: ranks whose
+    gradient-ready callbacks fire in different orders still finish."""
+    for seed in range(40):
+        run_zero(monkeypatch, 4, seed, units=5, shuffled=True)
         monkeypatch.undo()
 
 
