@@ -210,10 +210,11 @@ def test_grad_clipping_consistent_across_stages():
     assert max(abs(x - y) for x, y in zip(c0, c3)) < 1e-4
 
 
-@pytest.mark.parametrize("stage", [1, 3])
+@pytest.mark.parametrize("stage", [0, 1, 2, 3])
 def test_checkpoint_resume_is_exact(stage, tmp_path):
+    """2k steps in one run and k + save/load + k give bit-identical losses on the CPU."""
     for r in run_ranks(W.w_resume, 2, stage, str(tmp_path)):
-        assert r["full"][2:] == pytest.approx(r["resumed"], abs=1e-6), r
+        assert r["full"][2:] == r["resumed"], r
 
 
 @pytest.mark.parametrize("schedule", ["1f1b", "gpipe"])
