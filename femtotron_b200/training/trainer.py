@@ -186,9 +186,10 @@ class Trainer:
             return
         now = time.perf_counter()
         tok = self.tokens_per_step()
-        tps = float("nan")
         if self._last_log_time is not None:
             tps = tok * (self.global_step - self._last_log_step) / (now - self._last_log_time)
+        else:       # first record: no earlier wall-clock mark, use the step's own time
+            tps = tok / (step_ms / 1e3) if step_ms > 0 else 0.0
         self._last_log_time, self._last_log_step = now, self.global_step
         mem = torch.cuda.max_memory_allocated() / 2 ** 30 if self.device.type == "cuda" else 0.0
         rec = dict(info, step_ms_max=step_ms, tokens_per_s=tps, peak_mem_gb=mem, time=time.time())
