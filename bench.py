@@ -483,6 +483,9 @@ def run_reference(args):
 
 def main():
     args = parse()
+    if not torch.cuda.is_available():
+        emit({"impl": args.impl, "unavailable": "no CUDA device: the benchmark runs on B200 GPUs"})
+        sys.exit(0 if args.impl == "reference" else 1)
     if args.impl == "reference":
         run_reference(args)
     else:
