@@ -38,7 +38,12 @@ def log(msg: str) -> None:
 
 
 def _bool(x: str) -> bool:
-    return x.lower() in ("true", "1", "yes")
+    v = x.lower()
+    if v in ("true", "1", "yes", "on"):
+        return True
+    if v in ("false", "0", "no", "off"):
+        return False
+    raise argparse.ArgumentTypeError(f"expected true/false, got {x!r}")
 
 
 def parse_args(argv=None):
@@ -56,7 +61,8 @@ def parse_args(argv=None):
               "schedule", "metrics_path", "data_dir", "tokenizer"):
         p.add_argument(f"--{k}", type=str, default=None)
     for k in ("ac_enabled", "sequence_parallel", "synthetic_data"):
-        p.add_argument(f"--{k}", type=_bool, default=None)
+        # `--ac_enabled true|false` as in the reference's CLI, or the bare flag for true
+        p.add_argument(f"--{k}", type=_bool, nargs="?", const=True, default=None)
     return p.parse_args(argv)
 
 

@@ -123,3 +123,19 @@ def test_cli_pipeline_checkpoint_resume(tmp_path):
                           "--config", cfg, "--num_hidden_layers", "2"])
     hf = LlamaForCausalLM.from_pretrained(out)
     assert hf.config.num_hidden_layers == 2 and len(hf.model.layers) == 2
+
+
+def test_cli_runs_the_references_own_yaml(tmp_path):
+    """A reference user's config file works unchanged (its dataset and tokenizer need the
+    network, so synthetic tokens are switched on from the command line, as a bare flag)."""
+    import pytest
+    sys.path.insert(0, os.path.join(ROOT, "baseline"))
+    import install_reference
+    ref_yaml = os.path.join(install_reference.DEFAULT_SOURCE, "tiny_llama_debug.yaml")
+    if not os.path.isfile(ref_yaml):
+        pytest.skip("the reference's YAML is not on this machine")
+    out = _run(["--config", ref_yaml, "--train_steps", "2", "--warmup_steps", "1", "--log_interval", "1",
+                "--num_hidden_layers", "2", "--synthetic_data", "--checkpoint_dir", str(tmp_path / "ck")],
+               tmp_path)
+    assert out.returncode == 0, out.stdout[-2000:] + out.stderr[-3000:]
+    assert "tp=2" in out.stdout and "step      2/2" in out.stdout
