@@ -1,7 +1,11 @@
 import os
 import sys
 
-import pytest
+# separate hardware queues for the library's concurrent streams (read when the CUDA context
+# is created, so it is set before anything can create one; the package sets the same default)
+os.environ.setdefault("CUDA_DEVICE_MAX_CONNECTIONS", "32")
+
+import pytest  # noqa: E402
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 if ROOT not in sys.path:
