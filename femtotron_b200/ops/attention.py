@@ -5,6 +5,9 @@ packed [B*S, (nq+2nkv)*d] QKV projection.  They cover head sizes 64 and 128 with
 multiple of 128; other shapes on a GPU use PyTorch SDPA, and every such call is counted in
 ``SDPA_FALLBACKS`` and announced once with a warning (FT_STRICT_ATTN=1 raises instead), so a
 benchmark or a test can assert that the library never ran on its path.
+
+Replaces the reference's attention, which runs inside Hugging Face ``LlamaDecoderLayer``
+modules (femtotron/model/llama_partial_model.py:143-150) through PyTorch SDPA with GQA.
 """
 from __future__ import annotations
 

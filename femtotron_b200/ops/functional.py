@@ -1,5 +1,12 @@
 """Autograd functions of the LLaMA hot path, built on the sm_100a kernels.
 
+They replace what the reference runs through Hugging Face modules and ATen: the decoder
+layers' RMSNorm, RoPE, attention and SwiGLU (femtotron/model/llama_partial_model.py:143-157),
+the column/row-parallel ``F.linear`` calls (femtotron/parallel/tensor_parallel/linear.py:72,
+:206), and the LM-head loss, which the reference computes with ``F.cross_entropy`` on full-vocab
+logits gathered over TP (femtotron/model/llama.py:91-111,
+femtotron/parallel/tensor_parallel/comm_ops.py:72-82); here the loss is vocab-parallel.
+
 Gradient sinks
 --------------
 Weight gradients are written by the wgrad GEMM epilogue directly into their destination:

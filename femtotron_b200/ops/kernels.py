@@ -3,6 +3,11 @@
 The CPU branches restate the kernels' math in plain PyTorch.  They run the gloo/CPU tests
 and serve as the fp32 references of the GPU numerics tests; they are never used for CUDA
 tensors.
+
+Reference counterparts: the vocab-parallel embedding lookup
+(femtotron/parallel/tensor_parallel/embedding.py:57-77), the gradient-norm sum of squares of
+ClipGradNorm (femtotron/training/grad_transform.py:13-76), and ``torch.optim.AdamW`` inside
+MixedPrecisionManager.step (femtotron/training/mixed_precision_manager.py:318-331).
 """
 from __future__ import annotations
 

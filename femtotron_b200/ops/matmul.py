@@ -1,5 +1,8 @@
 """tcgen05 GEMM entry points and the three products of a linear layer.
 
+These replace the cuBLAS GEMMs behind the reference's ``F.linear`` calls
+(femtotron/parallel/tensor_parallel/linear.py:72 and :206) and their autograd backward.
+
 ``gemm`` computes ``D (op)= A @ B^T`` with A given as [M,K] (``a_mn=False``) or as its
 transpose [K,M] (``a_mn=True``), and B as [N,K] or [K,N] (``b_mn``).  On CUDA it runs the
 persistent tcgen05 kernel of ``csrc/gemm.cu``; on CPU the same contract is evaluated in

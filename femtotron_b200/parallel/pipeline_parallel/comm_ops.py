@@ -6,7 +6,10 @@ is ready), and the compute stream waits on the communication stream only when a 
 tensor is consumed — the host never blocks, so transfers overlap with compute already
 queued.  Combined send+recv operations are submitted together so neighbours can never
 deadlock in 1F1B's steady state.  Devices come from the parallel context (one process per
-local GPU), not from the global rank as in the reference (single-node only there)."""
+local GPU), not from the global rank as in the reference (single-node only there).
+
+Reference: ``PipelineComm`` (femtotron/parallel/pipeline_parallel/comm_ops.py:33-198), which
+issues ``batch_isend_irecv`` on the compute stream and waits on the host (:187-198)."""
 from __future__ import annotations
 
 from typing import Optional, Sequence

@@ -1,4 +1,5 @@
-"""Split a batch along dim 0 into equal micro-batches (views)."""
+"""Split a batch along dim 0 into equal micro-batches (views); reference:
+femtotron/parallel/pipeline_parallel/microbatch.py:16."""
 from __future__ import annotations
 
 import torch

@@ -1,3 +1,4 @@
+"""Pipeline settings (reference: femtotron/parallel/pipeline_parallel/pipeline_config.py:8)."""
 from __future__ import annotations
 
 from dataclasses import dataclass

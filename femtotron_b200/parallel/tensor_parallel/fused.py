@@ -23,6 +23,12 @@ Reduce-scatter (RS) of a row-parallel GEMM's partial output over tokens:
   2. the owner of rows [me*Tl, (me+1)*Tl) runs ``rs_pull``: it waits (bounded) for every
      PART flag, sums those rows of every peer's slot in fp32 over NVLink, adds the residual,
      writes bf16, and then the stream writes CONS[me] = e into every peer.
+These paths replace the reference's TP collectives around the column- and row-parallel
+linears (femtotron/parallel/tensor_parallel/linear.py:66-77, :194-210): the backward
+all-reduce of ``CopyToTPRegion`` and the forward all-reduce of ``ReduceFromTPRegion``
+(femtotron/parallel/tensor_parallel/comm_ops.py:33, :117), which the reference issues with no
+sequence parallelism.
+
 Slots are double-buffered per direction; epochs increase monotonically and every rank makes
 the same sequence of calls, so stale flags are never mistaken for fresh ones.
 

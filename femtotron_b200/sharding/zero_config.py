@@ -1,3 +1,5 @@
+"""ZeRO configuration: the reference's fields (femtotron/sharding/zero_config.py:8) plus
+``prefetch`` for the ZeRO-3 parameter gathers."""
 from __future__ import annotations
 
 from dataclasses import dataclass
